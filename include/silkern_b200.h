@@ -1,0 +1,155 @@
+/*
+ * silkern_b200 -- C ABI of the B200 (sm_100a) sparse-index localization converter.
+ *
+ * The converter turns one selection batch of global logical token positions
+ * (batch, width) int32 into the rank-local physical KV slots that one decode
+ * context-parallel (DCP) rank owns, compacted to the front of each row in the
+ * selector's order, plus an exact valid count per row.
+ *
+ * Per element t of row r (request q = req_ids[r], table row = block_table[q]):
+ *   owner = (t / interleave) % dcp_size                       (t >= 0 only)
+ *   local = (t / (dcp_size * interleave)) * interleave + t % interleave
+ *   lb, off = local / block_size, local % block_size
+ *   valid  = t >= 0 && owner == dcp_rank && lb < table_width
+ *   phys   = block_table[q][lb] * block_size + off            (int32 wrap)
+ * With compaction (compact_valid_to_front && dcp_size > 1) the valid values
+ * fill out[r][0:count] in input order and the rest of the row is -1; without
+ * it every column keeps its own value (phys, or -1 when invalid).
+ *
+ * Conventions shared by every entry point:
+ *   - every buffer is caller-owned int32 device memory, contiguous, on the
+ *     device that is current on the calling thread; nothing is allocated and
+ *     nothing is synchronised, so calls may be captured in a CUDA graph;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream);
+ *   - launches use programmatic dependent launch: each kernel waits on the
+ *     previous grid in the stream before it reads any input;
+ *   - `status` may be NULL; otherwise a row whose request id is outside
+ *     [0, table_rows) is emitted as all -1 with count 0 and the kernel stores
+ *     SILKERN_STATUS_BAD_REQUEST into *status (it never clears it);
+ *   - return value: 0 on success, a positive SILKERN_E* code when an argument
+ *     is rejected before launch (nothing is enqueued), or -(cudaError_t) when
+ *     the launch itself fails.
+ */
+#ifndef SILKERN_B200_H_
+#define SILKERN_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SILKERN_ABI_VERSION 1
+
+#define SILKERN_OK 0
+#define SILKERN_E_NULL 1         /* a required pointer is NULL */
+#define SILKERN_E_SHAPE 2        /* batch/width/table dimensions out of range */
+#define SILKERN_E_DCP 3          /* invalid dcp_size / dcp_rank / interleave */
+#define SILKERN_E_BLOCK_SIZE 4   /* block_size < 1 or not divisible by interleave */
+#define SILKERN_E_TILE 5         /* unsupported tile_size */
+#define SILKERN_E_ALIAS 6        /* an output overlaps an input or another output */
+#define SILKERN_E_GEOMETRY 7     /* explicit launch geometry rejected */
+
+#define SILKERN_STATUS_BAD_REQUEST 1
+
+/* Widest selection row either entry point accepts. */
+#define SILKERN_MAX_ROW_WIDTH 16384
+/* Hierarchical tile sizes accepted by the workspace geometry. */
+#define SILKERN_MIN_TILE_SIZE 64
+#define SILKERN_MAX_TILE_SIZE 1024
+
+/*
+ * Row-wise stable localization: one launch; each row is scanned by one CTA
+ * (or, for long rows with few requests, by a thread-block cluster that
+ * exchanges per-CTA counts through distributed shared memory).
+ * Replaces silkern/kernels.py:318-434 (localize_rowwise and _rowwise_kernel,
+ * kernels.py:51-125). block_table is (table_rows, table_width); tokens and
+ * out are (batch, width); req_ids and counts are (batch,).
+ */
+int silkern_localize_rowwise_v1(const int32_t* req_ids, const int32_t* block_table,
+                                int64_t table_rows, int64_t table_width,
+                                const int32_t* tokens, int32_t* out, int32_t* counts,
+                                int64_t batch, int64_t width, int32_t block_size,
+                                int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave,
+                                int32_t compact_valid_to_front, int32_t* status,
+                                void* stream);
+
+/*
+ * Hierarchical stable localization for wide rows: each row is split into
+ * tiles of tile_size columns; the CTAs of one row form a thread-block cluster,
+ * compose their tile-prefix offsets deterministically (no atomics) and
+ * publish them into the caller-owned workspace: tile_counts[r][k] is the
+ * number of valid elements in tile k and tile_offsets[r][k] the exclusive
+ * prefix of those counts, both (batch, ceil(width / tile_size)).
+ * mapped_ws and local_positions_ws, (batch, width), are accepted for
+ * interface compatibility and are neither read nor written (may be NULL).
+ * Replaces silkern/kernels.py:436-633 (localize_hierarchical and the
+ * _map_tiles / _tile_prefix / _fill_output / _scatter_tiles kernels,
+ * kernels.py:127-315).
+ */
+int silkern_localize_hierarchical_v1(const int32_t* req_ids, const int32_t* block_table,
+                                     int64_t table_rows, int64_t table_width,
+                                     const int32_t* tokens, int32_t* out, int32_t* counts,
+                                     int32_t* mapped_ws, int32_t* local_positions_ws,
+                                     int32_t* tile_counts_ws, int32_t* tile_offsets_ws,
+                                     int64_t batch, int64_t width, int32_t block_size,
+                                     int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave,
+                                     int32_t compact_valid_to_front, int32_t tile_size,
+                                     int32_t* status, void* stream);
+
+/*
+ * Exact caller-owned workspace shapes for the hierarchical entry point, as
+ * four (rows, cols) pairs in the order mapped, local_positions, tile_counts,
+ * tile_offsets. Host only; touches no device. Replaces
+ * silkern/workspace.py:22-53 (workspace_shapes).
+ */
+int silkern_workspace_shapes_v1(int64_t batch, int64_t width, int32_t tile_size,
+                                int64_t out_shapes[8]);
+
+/*
+ * Row-wise or hierarchical localization with an explicit launch geometry, for
+ * conformance sweeps and tuning: cluster_size CTAs per row (1, 2, 4 or 8),
+ * stage_table = 1 stages the request's block-table row in shared memory
+ * (table_width <= 4096), 0 gathers it from global memory, -1 lets the
+ * library decide; prefetch_table likewise for the L2 bulk prefetch of the
+ * whole table. tile_size = 0 selects row-wise semantics (no workspace).
+ * Same semantics and outputs as the entry points above. No counterpart in the
+ * reference (its launch geometry is fixed inside each launcher).
+ */
+int silkern_localize_explicit_v1(const int32_t* req_ids, const int32_t* block_table,
+                                 int64_t table_rows, int64_t table_width,
+                                 const int32_t* tokens, int32_t* out, int32_t* counts,
+                                 int32_t* tile_counts_ws, int32_t* tile_offsets_ws,
+                                 int64_t batch, int64_t width, int32_t block_size,
+                                 int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave,
+                                 int32_t compact_valid_to_front, int32_t tile_size,
+                                 int32_t cluster_size, int32_t stage_table,
+                                 int32_t prefetch_table, int32_t* status, void* stream);
+
+/*
+ * Device-side equality check used by the CUDA-graph replay gate: adds the
+ * number of positions i < n with a[i] != b[i] to *mismatches (one atomic add
+ * per CTA). No counterpart in the reference (its replay check copies to the
+ * host, silkern/verify.py:362-372).
+ */
+int silkern_count_mismatches_v1(const int32_t* a, const int32_t* b, int64_t n,
+                                int32_t* mismatches, void* stream);
+
+/* Static text for a return code (positive SILKERN_E*, 0, or -cudaError_t). */
+const char* silkern_status_string_v1(int code);
+
+/* SILKERN_ABI_VERSION of the loaded library. */
+int silkern_abi_version_v1(void);
+
+/*
+ * Host check of the invariant-divisor division the kernels use: returns the
+ * number of n in [n_begin, n_begin + n_count) (all < 2^31) for which the fast
+ * quotient differs from n / divisor. Test hook; touches no device.
+ */
+int64_t silkern_fastdiv_selftest_v1(uint32_t divisor, uint32_t n_begin, uint32_t n_count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SILKERN_B200_H_ */

@@ -1,0 +1,698 @@
+// Sparse-index localization for decode context parallelism on B200 (sm_100a).
+//
+// One kernel serves both public entry points. A row of `width` selected token
+// positions is split into `cluster` contiguous column slices; each slice is
+// one CTA, and the CTAs of one row form a thread-block cluster (cluster == 1
+// for the common row-wise case). Per CTA:
+//
+//   1. read the row's request id and the slice's tokens with 128-bit loads
+//      (scalar loads only when the slice start is not 16-byte aligned);
+//   2. stage the request's block-table row in shared memory (or gather it
+//      from global memory when the row is wide);
+//   3. apply ownership, deinterleave and paged translation with shifts (all
+//      powers of two) or invariant-divisor multiplies (general case);
+//   4. stable compaction: warp ballots give each lane its prefix inside the
+//      warp, warp totals go through shared memory and a redux.sync per chunk
+//      gives each warp its base; across a cluster, each CTA pushes its total
+//      into every CTA's shared memory (DSMEM) before one cluster barrier.
+//      No atomics, so the order is the selector's order on every run;
+//   5. survivors are staged per warp and written with consecutive stores,
+//      the -1 tail with 128-bit stores; every output element is written
+//      exactly once.
+//
+// Semantics follow silkern/contract.py:67-158 (localize_reference) and the
+// int32 lanes of silkern/kernels.py:51-125 (_rowwise_kernel).
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "fastdiv.cuh"
+#include "ptx.cuh"
+#include "silkern_b200.h"
+
+namespace silkern {
+
+constexpr int kMaxThreads = 1024;
+constexpr int kMaxCluster = 8;
+constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
+constexpr int kWarpStage = 128;       // survivors one warp stages per chunk (32 lanes x 4)
+constexpr uint32_t kFull = 0xffffffffu;
+
+struct Params {
+  const int32_t* req_ids;
+  const int32_t* table;
+  const int32_t* tokens;
+  int32_t* out;
+  int32_t* counts;
+  int32_t* tile_counts;   // hierarchical workspace, or nullptr
+  int32_t* tile_offsets;  // hierarchical workspace, or nullptr
+  int32_t* status;        // optional error word
+  int64_t table_rows;
+  uint32_t table_width;
+  int32_t width;
+  int32_t slice;          // columns per CTA (multiple of 4, or of tile_size)
+  int32_t cluster;        // CTAs per row
+  int32_t stage_entries;  // table entries staged in shared memory (0: gather)
+  int32_t compact;
+  int32_t tile_shift;     // log2(tile_size) when publishing tiles, else -1
+  int32_t tiles_per_row;
+  uint32_t prefetch_bytes;  // L2 prefetch: table bytes (multiple of 16), 0 = off
+  uint32_t dcp_rank;
+  uint32_t dcp_size;
+  uint32_t interleave;
+  uint32_t block_size;
+  // general path
+  FastDiv div_il, div_dcp, div_bs;
+  // all-powers-of-two path
+  uint32_t il_shift, group_shift, bs_shift;
+  uint32_t il_mask, dcp_mask, bs_mask;
+};
+
+// Ownership + deinterleave + logical block of one non-negative token.
+template <bool POW2>
+__device__ __forceinline__ bool locate(uint32_t u, const Params& p, uint32_t& lb, uint32_t& off) {
+  uint32_t owner, local;
+  if constexpr (POW2) {
+    owner = (u >> p.il_shift) & p.dcp_mask;
+    local = ((u >> p.group_shift) << p.il_shift) | (u & p.il_mask);
+    lb = local >> p.bs_shift;
+    off = local & p.bs_mask;
+  } else {
+    const uint32_t q1 = fastdiv(u, p.div_il);   // t / interleave
+    const uint32_t r1 = u - q1 * p.interleave;  // t % interleave
+    const uint32_t q2 = fastdiv(q1, p.div_dcp);  // t / (dcp_size * interleave)
+    owner = q1 - q2 * p.dcp_size;                // (t / interleave) % dcp_size
+    local = q2 * p.interleave + r1;
+    lb = fastdiv(local, p.div_bs);
+    off = local - lb * p.block_size;
+  }
+  return owner == p.dcp_rank && lb < p.table_width;
+}
+
+// out[lo:hi] = -1 with 128-bit stores on the aligned body.
+__device__ __forceinline__ void fill_invalid(int32_t* row, int lo, int hi, int tid, int nthreads) {
+  if (lo >= hi) return;
+  int32_t* dst = row + lo;
+  const int n = hi - lo;
+  int head = static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 2);
+  head = head < n ? head : n;
+  if (tid < head) dst[tid] = -1;
+  const int nvec = (n - head) >> 2;
+  int4* body = reinterpret_cast<int4*>(dst + head);
+  for (int g = tid; g < nvec; g += nthreads) body[g] = make_int4(-1, -1, -1, -1);
+  const int rest = n - head - 4 * nvec;
+  if (tid < rest) dst[head + 4 * nvec + tid] = -1;
+}
+
+template <int NC, bool POW2>
+__global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(16) int32_t smem[];
+  __shared__ int32_t s_cta_total[kMaxCluster];
+
+  const int nthreads = blockDim.x;
+  const int nwarps = nthreads >> 5;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int cs = p.cluster;
+  const int64_t row = blockIdx.x / static_cast<uint32_t>(cs);
+  const int crank = static_cast<int>(blockIdx.x - row * cs);
+
+  int32_t* s_tbl = smem;
+  int32_t* s_wt = s_tbl + p.stage_entries;  // [NC][32] warp totals
+  int32_t* s_stage = s_wt + NC * 32;        // [nwarps][kWarpStage]
+  int32_t* s_tile = s_stage + nwarps * kWarpStage;
+
+  if (cs > 1) cluster_arrive_relaxed();  // phase 0: this CTA is resident
+
+  pdl_wait();
+  pdl_launch_dependents();
+
+  if (p.prefetch_bytes != 0 && tid == 0) {
+    // Each CTA warms L2 with its share of the whole block table while the
+    // request id (on which its own table row depends) is still in flight.
+    const uint64_t total = p.prefetch_bytes;
+    const uint64_t nblk = gridDim.x;
+    const uint64_t chunk = (((total + nblk - 1) / nblk) + 15u) & ~uint64_t{15};
+    const uint64_t begin = blockIdx.x * chunk;
+    if (begin < total) {
+      const uint64_t end = begin + chunk < total ? begin + chunk : total;
+      prefetch_l2_bulk(reinterpret_cast<const char*>(p.table) + begin, static_cast<uint32_t>(end - begin));
+    }
+  }
+
+  const int32_t req = __ldg(p.req_ids + row);
+
+  const int c0 = crank * p.slice;
+  const int len = min(p.slice, p.width - c0);
+  const int32_t* tok = p.tokens + row * p.width + c0;
+  const bool tok_vec = (reinterpret_cast<uintptr_t>(tok) & 15u) == 0;
+
+  int32_t val[NC][4];
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int col = 4 * (i * nthreads + tid);
+    if (tok_vec && col + 4 <= len) {
+      const int4 q = __ldg(reinterpret_cast<const int4*>(tok + col));
+      val[i][0] = q.x;
+      val[i][1] = q.y;
+      val[i][2] = q.z;
+      val[i][3] = q.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) val[i][j] = (col + j < len) ? __ldg(tok + col + j) : -1;
+    }
+  }
+
+  const bool req_ok = req >= 0 && static_cast<int64_t>(req) < p.table_rows;
+  if (!req_ok && p.status != nullptr && tid == 0) {
+    *reinterpret_cast<volatile int32_t*>(p.status) = SILKERN_STATUS_BAD_REQUEST;
+  }
+  const int32_t* trow = p.table + static_cast<int64_t>(req_ok ? req : 0) * p.table_width;
+
+  if (p.stage_entries != 0) {
+    if (req_ok) {
+      const int n = p.stage_entries;
+      if ((reinterpret_cast<uintptr_t>(trow) & 15u) == 0) {
+        const int nvec = n >> 2;
+        const int4* src = reinterpret_cast<const int4*>(trow);
+        int4* dst = reinterpret_cast<int4*>(s_tbl);
+        for (int g = tid; g < nvec; g += nthreads) dst[g] = __ldg(src + g);
+        for (int e = 4 * nvec + tid; e < n; e += nthreads) s_tbl[e] = __ldg(trow + e);
+      } else {
+        for (int e = tid; e < n; e += nthreads) s_tbl[e] = __ldg(trow + e);
+      }
+    }
+    __syncthreads();
+  }
+
+  // Map every element; val becomes the physical slot (or -1), bits[i] marks
+  // the valid ones.
+  uint32_t bits[NC];
+  int lane_pre[NC];
+  int warp_tot[NC];
+  const uint32_t lt = lanemask_lt();
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    uint32_t b = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int32_t t = val[i][j];
+      int32_t phys = -1;
+      uint32_t lb, off;
+      if (t >= 0 && req_ok && locate<POW2>(static_cast<uint32_t>(t), p, lb, off)) {
+        const int32_t blk = p.stage_entries != 0 ? s_tbl[lb] : __ldg(trow + lb);
+        phys = static_cast<int32_t>(static_cast<uint32_t>(blk) * p.block_size + off);
+        b |= 1u << j;
+      }
+      val[i][j] = phys;
+    }
+    bits[i] = b;
+    const uint32_t b0 = __ballot_sync(kFull, b & 1u);
+    const uint32_t b1 = __ballot_sync(kFull, b & 2u);
+    const uint32_t b2 = __ballot_sync(kFull, b & 4u);
+    const uint32_t b3 = __ballot_sync(kFull, b & 8u);
+    lane_pre[i] = __popc(b0 & lt) + __popc(b1 & lt) + __popc(b2 & lt) + __popc(b3 & lt);
+    warp_tot[i] = __popc(b0) + __popc(b1) + __popc(b2) + __popc(b3);
+    if (lane == 0) s_wt[i * 32 + warp] = warp_tot[i];
+  }
+  __syncthreads();
+
+  // Exclusive base of (chunk i, this warp) inside the CTA: all earlier chunks,
+  // then the earlier warps of chunk i.
+  int base[NC];
+  int run = 0;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int x = lane < nwarps ? s_wt[i * 32 + lane] : 0;
+    const int before = __reduce_add_sync(kFull, lane < warp ? x : 0);
+    const int tot = __reduce_add_sync(kFull, x);
+    base[i] = run + before;
+    run += tot;
+  }
+  const int cta_total = run;
+
+  int row_off = 0;
+  int row_total = cta_total;
+  if (cs > 1) {
+    cluster_wait_acquire();  // phase 0 complete: every CTA of the cluster runs
+    if (tid < cs) st_shared_cluster(&s_cta_total[crank], static_cast<uint32_t>(tid), cta_total);
+    cluster_arrive_release();
+    cluster_wait_acquire();  // phase 1: every CTA's total is in s_cta_total
+    row_total = 0;
+    for (int r = 0; r < cs; ++r) {
+      const int v = s_cta_total[r];
+      row_off += r < crank ? v : 0;
+      row_total += v;
+    }
+  }
+
+  int32_t* orow = p.out + row * p.width;
+  if (p.compact) {
+    int32_t* stage = s_stage + warp * kWarpStage;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      int pos = lane_pre[i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (bits[i] & (1u << j)) stage[pos++] = val[i][j];
+      }
+      __syncwarp();
+      const int n = warp_tot[i];
+      int32_t* dst = orow + row_off + base[i];
+      for (int e = lane; e < n; e += 32) dst[e] = stage[e];
+      __syncwarp();
+    }
+    fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
+  } else {
+    int32_t* dst = orow + c0;
+    const bool out_vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int col = 4 * (i * nthreads + tid);
+      if (out_vec && col + 4 <= len) {
+        *reinterpret_cast<int4*>(dst + col) = make_int4(val[i][0], val[i][1], val[i][2], val[i][3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (col + j < len) dst[col + j] = val[i][j];
+        }
+      }
+    }
+  }
+
+  if (p.tile_shift >= 0) {
+    // Publish the tile decomposition: the exclusive position of the element
+    // in a tile's first column is that tile's offset; counts are differences.
+    const int tmask = (1 << p.tile_shift) - 1;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int col = 4 * (i * nthreads + tid);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (col + j < len && ((col + j) & tmask) == 0) {
+          s_tile[(col + j) >> p.tile_shift] =
+              row_off + base[i] + lane_pre[i] + __popc(bits[i] & ((1u << j) - 1u));
+        }
+      }
+    }
+    __syncthreads();
+    const int ntiles = (len + tmask) >> p.tile_shift;
+    const int cta_end = row_off + cta_total;
+    const int64_t tbase = row * p.tiles_per_row + (c0 >> p.tile_shift);
+    for (int m = tid; m < ntiles; m += nthreads) {
+      const int o = s_tile[m];
+      const int next = m + 1 < ntiles ? s_tile[m + 1] : cta_end;
+      p.tile_offsets[tbase + m] = o;
+      p.tile_counts[tbase + m] = next - o;
+    }
+  }
+
+  if (crank == 0 && tid == 0) p.counts[row] = row_total;
+}
+
+// Adds the number of differing positions to *mismatches.
+__global__ void __launch_bounds__(256) count_mismatches_kernel(const int32_t* a, const int32_t* b,
+                                                               int64_t n, int32_t* mismatches) {
+  __shared__ int s_part[8];
+  pdl_wait();
+  pdl_launch_dependents();
+  int local = 0;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    local += a[i] != b[i] ? 1 : 0;
+  }
+  local = __reduce_add_sync(kFull, local);
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = local;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int total = 0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) total += s_part[w];
+    if (total != 0) atomicAdd(mismatches, total);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+namespace {
+
+using KernelFn = void (*)(Params);
+
+KernelFn pick_kernel(int nc, bool pow2) {
+  switch (nc) {
+    case 1: return pow2 ? localize_kernel<1, true> : localize_kernel<1, false>;
+    case 2: return pow2 ? localize_kernel<2, true> : localize_kernel<2, false>;
+    case 4: return pow2 ? localize_kernel<4, true> : localize_kernel<4, false>;
+    default: return nullptr;
+  }
+}
+
+bool is_pow2(uint32_t v) { return v != 0 && (v & (v - 1)) == 0; }
+
+uint32_t log2_exact(uint32_t v) {
+  uint32_t s = 0;
+  while ((1u << s) < v) ++s;
+  return s;
+}
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+bool overlaps(const void* a, int64_t a_elems, const void* b, int64_t b_elems) {
+  if (a == nullptr || b == nullptr) return false;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  const uintptr_t a1 = a0 + static_cast<uintptr_t>(a_elems) * 4u;
+  const uintptr_t b1 = b0 + static_cast<uintptr_t>(b_elems) * 4u;
+  return a0 < b1 && b0 < a1;
+}
+
+struct Request {
+  const int32_t* req_ids;
+  const int32_t* table;
+  int64_t table_rows, table_width;
+  const int32_t* tokens;
+  int32_t* out;
+  int32_t* counts;
+  int32_t* tile_counts;
+  int32_t* tile_offsets;
+  int64_t batch, width;
+  int32_t block_size, dcp_size, dcp_rank, interleave, compact_flag;
+  int32_t tile_size;  // 0 = row-wise semantics
+  int32_t* status;
+  cudaStream_t stream;
+};
+
+int validate(const Request& r) {
+  if (!r.req_ids || !r.table || !r.tokens || !r.out || !r.counts) return SILKERN_E_NULL;
+  if (r.batch < 1 || r.width < 1 || r.width > SILKERN_MAX_ROW_WIDTH || r.table_rows < 1 ||
+      r.table_width < 1 || r.table_width > INT32_MAX || r.batch > (int64_t{1} << 27)) {
+    return SILKERN_E_SHAPE;
+  }
+  if (r.dcp_size < 1 || r.dcp_rank < 0 || r.dcp_rank >= r.dcp_size || r.interleave < 1) return SILKERN_E_DCP;
+  if (r.block_size < 1 || r.block_size % r.interleave != 0) return SILKERN_E_BLOCK_SIZE;
+  if (r.tile_size != 0) {
+    if (r.tile_size < SILKERN_MIN_TILE_SIZE || r.tile_size > SILKERN_MAX_TILE_SIZE ||
+        !is_pow2(static_cast<uint32_t>(r.tile_size))) {
+      return SILKERN_E_TILE;
+    }
+    if (!r.tile_counts || !r.tile_offsets) return SILKERN_E_NULL;
+  }
+  const int64_t bw = r.batch * r.width;
+  const int64_t tiles = r.tile_size ? r.batch * ((r.width + r.tile_size - 1) / r.tile_size) : 0;
+  struct Range { const void* p; int64_t n; };
+  const Range inputs[3] = {{r.req_ids, r.batch}, {r.table, r.table_rows * r.table_width}, {r.tokens, bw}};
+  const Range outputs[4] = {{r.out, bw}, {r.counts, r.batch}, {r.tile_counts, tiles}, {r.tile_offsets, tiles}};
+  for (const Range& o : outputs) {
+    for (const Range& in : inputs) {
+      if (overlaps(o.p, o.n, in.p, in.n)) return SILKERN_E_ALIAS;
+    }
+  }
+  for (int a = 0; a < 4; ++a) {
+    for (int b = a + 1; b < 4; ++b) {
+      if (overlaps(outputs[a].p, outputs[a].n, outputs[b].p, outputs[b].n)) return SILKERN_E_ALIAS;
+    }
+  }
+  return SILKERN_OK;
+}
+
+struct Geometry {
+  int cluster;
+  int slice;
+  int threads;
+  int nc;
+  bool stage;
+  bool prefetch;
+};
+
+// Chunks per thread and threads per CTA for a slice of `slice` columns.
+bool fit_slice(int slice, int* nc, int* threads) {
+  const int granules = (slice + 3) / 4;
+  int c = 1;
+  while (granules > c * kMaxThreads) c *= 2;
+  if (c > 4) return false;
+  int t = (granules + c - 1) / c;
+  t = (t + 31) / 32 * 32;
+  *nc = c;
+  *threads = t;
+  return true;
+}
+
+int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefetch_req, Geometry* g) {
+  const int width = static_cast<int>(r.width);
+  int cs;
+  int slice;
+  if (r.tile_size != 0) {
+    // Hierarchical: a CTA covers a whole number of tiles, at most 8 CTAs/row.
+    const int tiles = (width + r.tile_size - 1) / r.tile_size;
+    int per_cta;
+    if (cluster_req > 0) {
+      per_cta = (tiles + cluster_req - 1) / cluster_req;
+    } else {
+      per_cta = (tiles + kMaxCluster - 1) / kMaxCluster;
+    }
+    slice = per_cta * r.tile_size;
+    cs = (tiles + per_cta - 1) / per_cta;
+  } else {
+    if (cluster_req > 0) {
+      cs = cluster_req;
+    } else {
+      // Row-wise: split long rows across a cluster only when there are too
+      // few rows to occupy the SMs.
+      const int sms = sm_count();
+      cs = 1;
+      while (cs < kMaxCluster && r.batch * cs < sms && width / (2 * cs) >= 1024) cs *= 2;
+    }
+    slice = (width + cs - 1) / cs;
+    slice = (slice + 3) / 4 * 4;
+    cs = (width + slice - 1) / slice;
+  }
+  if (cluster_req > 0 && cs != cluster_req) return SILKERN_E_GEOMETRY;
+  if (cs < 1 || cs > kMaxCluster) return SILKERN_E_GEOMETRY;
+  if (!fit_slice(slice, &g->nc, &g->threads)) return SILKERN_E_GEOMETRY;
+  g->cluster = cs;
+  g->slice = slice;
+  if (stage_req == 1 && r.table_width > kTableStageMax) return SILKERN_E_GEOMETRY;
+  g->stage = stage_req >= 0 ? stage_req == 1 : r.table_width <= kTableStageMax;
+  const int64_t table_bytes = r.table_rows * r.table_width * 4;
+  const bool aligned = (reinterpret_cast<uintptr_t>(r.table) & 15u) == 0;
+  bool prefetch = aligned && table_bytes >= 16 && table_bytes <= 2 * r.batch * r.width * 4 &&
+                  table_bytes <= (int64_t{1} << 31);
+  if (prefetch_req >= 0) prefetch = prefetch_req == 1 && aligned && table_bytes >= 16 &&
+                                    table_bytes <= (int64_t{1} << 31);
+  g->prefetch = prefetch;
+  if (r.batch * cs > INT32_MAX) return SILKERN_E_SHAPE;
+  return SILKERN_OK;
+}
+
+int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req) {
+  int rc = validate(r);
+  if (rc != SILKERN_OK) return rc;
+  Geometry g;
+  rc = choose_geometry(r, cluster_req, stage_req, prefetch_req, &g);
+  if (rc != SILKERN_OK) return rc;
+
+  Params p{};
+  p.req_ids = r.req_ids;
+  p.table = r.table;
+  p.tokens = r.tokens;
+  p.out = r.out;
+  p.counts = r.counts;
+  p.tile_counts = r.tile_counts;
+  p.tile_offsets = r.tile_offsets;
+  p.status = r.status;
+  p.table_rows = r.table_rows;
+  p.table_width = static_cast<uint32_t>(r.table_width);
+  p.width = static_cast<int32_t>(r.width);
+  p.slice = g.slice;
+  p.cluster = g.cluster;
+  p.stage_entries = g.stage ? static_cast<int32_t>(r.table_width) : 0;
+  p.compact = (r.compact_flag != 0 && r.dcp_size > 1) ? 1 : 0;
+  p.tile_shift = r.tile_size ? static_cast<int32_t>(log2_exact(static_cast<uint32_t>(r.tile_size))) : -1;
+  p.tiles_per_row = r.tile_size ? static_cast<int32_t>((r.width + r.tile_size - 1) / r.tile_size) : 0;
+  const int64_t table_bytes = r.table_rows * r.table_width * 4;
+  p.prefetch_bytes = g.prefetch ? static_cast<uint32_t>(table_bytes & ~int64_t{15}) : 0u;
+  p.dcp_rank = static_cast<uint32_t>(r.dcp_rank);
+  p.dcp_size = static_cast<uint32_t>(r.dcp_size);
+  p.interleave = static_cast<uint32_t>(r.interleave);
+  p.block_size = static_cast<uint32_t>(r.block_size);
+  p.div_il = make_fastdiv(p.interleave);
+  p.div_dcp = make_fastdiv(p.dcp_size);
+  p.div_bs = make_fastdiv(p.block_size);
+  const bool pow2 = is_pow2(p.interleave) && is_pow2(p.dcp_size) && is_pow2(p.block_size) &&
+                    log2_exact(p.interleave) + log2_exact(p.dcp_size) <= 31;
+  if (pow2) {
+    p.il_shift = log2_exact(p.interleave);
+    p.group_shift = p.il_shift + log2_exact(p.dcp_size);
+    p.bs_shift = log2_exact(p.block_size);
+    p.il_mask = p.interleave - 1;
+    p.dcp_mask = p.dcp_size - 1;
+    p.bs_mask = p.block_size - 1;
+  }
+
+  KernelFn fn = pick_kernel(g.nc, pow2);
+  if (fn == nullptr) return SILKERN_E_GEOMETRY;
+  const int nwarps = g.threads / 32;
+  const int ntiles_cta = r.tile_size ? (g.slice + r.tile_size - 1) / r.tile_size : 0;
+  const size_t smem = sizeof(int32_t) * (static_cast<size_t>(p.stage_entries) + g.nc * 32 +
+                                         static_cast<size_t>(nwarps) * kWarpStage + ntiles_cta);
+
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(r.batch * g.cluster), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(g.threads), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = r.stream;
+  cudaLaunchAttribute attrs[2];
+  int nattr = 0;
+  attrs[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[nattr].val.programmaticStreamSerializationAllowed = 1;
+  ++nattr;
+  if (g.cluster > 1) {
+    attrs[nattr].id = cudaLaunchAttributeClusterDimension;
+    attrs[nattr].val.clusterDim.x = static_cast<unsigned>(g.cluster);
+    attrs[nattr].val.clusterDim.y = 1;
+    attrs[nattr].val.clusterDim.z = 1;
+    ++nattr;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = nattr;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, fn, p);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -static_cast<int>(err);
+  }
+  return SILKERN_OK;
+}
+
+}  // namespace
+}  // namespace silkern
+
+using silkern::Request;
+
+extern "C" int silkern_localize_rowwise_v1(const int32_t* req_ids, const int32_t* block_table,
+                                           int64_t table_rows, int64_t table_width,
+                                           const int32_t* tokens, int32_t* out, int32_t* counts,
+                                           int64_t batch, int64_t width, int32_t block_size,
+                                           int32_t dcp_size, int32_t dcp_rank,
+                                           int32_t dcp_interleave, int32_t compact_valid_to_front,
+                                           int32_t* status, void* stream) {
+  const Request r{req_ids, block_table, table_rows, table_width, tokens, out, counts, nullptr, nullptr,
+                  batch, width, block_size, dcp_size, dcp_rank, dcp_interleave,
+                  compact_valid_to_front, 0, status, static_cast<cudaStream_t>(stream)};
+  return silkern::launch(r, 0, -1, -1);
+}
+
+extern "C" int silkern_localize_hierarchical_v1(
+    const int32_t* req_ids, const int32_t* block_table, int64_t table_rows, int64_t table_width,
+    const int32_t* tokens, int32_t* out, int32_t* counts, int32_t* mapped_ws,
+    int32_t* local_positions_ws, int32_t* tile_counts_ws, int32_t* tile_offsets_ws, int64_t batch,
+    int64_t width, int32_t block_size, int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave,
+    int32_t compact_valid_to_front, int32_t tile_size, int32_t* status, void* stream) {
+  (void)mapped_ws;
+  (void)local_positions_ws;
+  if (tile_size == 0) return SILKERN_E_TILE;
+  const Request r{req_ids, block_table, table_rows, table_width, tokens, out, counts,
+                  tile_counts_ws, tile_offsets_ws, batch, width, block_size, dcp_size, dcp_rank,
+                  dcp_interleave, compact_valid_to_front, tile_size, status,
+                  static_cast<cudaStream_t>(stream)};
+  return silkern::launch(r, 0, -1, -1);
+}
+
+extern "C" int silkern_localize_explicit_v1(
+    const int32_t* req_ids, const int32_t* block_table, int64_t table_rows, int64_t table_width,
+    const int32_t* tokens, int32_t* out, int32_t* counts, int32_t* tile_counts_ws,
+    int32_t* tile_offsets_ws, int64_t batch, int64_t width, int32_t block_size, int32_t dcp_size,
+    int32_t dcp_rank, int32_t dcp_interleave, int32_t compact_valid_to_front, int32_t tile_size,
+    int32_t cluster_size, int32_t stage_table, int32_t prefetch_table, int32_t* status,
+    void* stream) {
+  if (cluster_size < 1 || cluster_size > silkern::kMaxCluster) return SILKERN_E_GEOMETRY;
+  if (stage_table < -1 || stage_table > 1 || prefetch_table < -1 || prefetch_table > 1) {
+    return SILKERN_E_GEOMETRY;
+  }
+  const Request r{req_ids, block_table, table_rows, table_width, tokens, out, counts,
+                  tile_counts_ws, tile_offsets_ws, batch, width, block_size, dcp_size, dcp_rank,
+                  dcp_interleave, compact_valid_to_front, tile_size, status,
+                  static_cast<cudaStream_t>(stream)};
+  return silkern::launch(r, cluster_size, stage_table, prefetch_table);
+}
+
+extern "C" int silkern_workspace_shapes_v1(int64_t batch, int64_t width, int32_t tile_size,
+                                           int64_t out_shapes[8]) {
+  if (out_shapes == nullptr) return SILKERN_E_NULL;
+  if (batch < 1 || width < 1 || width > SILKERN_MAX_ROW_WIDTH) return SILKERN_E_SHAPE;
+  if (tile_size < SILKERN_MIN_TILE_SIZE || tile_size > SILKERN_MAX_TILE_SIZE ||
+      !silkern::is_pow2(static_cast<uint32_t>(tile_size))) {
+    return SILKERN_E_TILE;
+  }
+  const int64_t tiles = (width + tile_size - 1) / tile_size;
+  const int64_t shapes[8] = {batch, width, batch, width, batch, tiles, batch, tiles};
+  for (int i = 0; i < 8; ++i) out_shapes[i] = shapes[i];
+  return SILKERN_OK;
+}
+
+extern "C" int silkern_count_mismatches_v1(const int32_t* a, const int32_t* b, int64_t n,
+                                           int32_t* mismatches, void* stream) {
+  if (!a || !b || !mismatches) return SILKERN_E_NULL;
+  if (n < 0) return SILKERN_E_SHAPE;
+  if (n == 0) return SILKERN_OK;
+  int64_t blocks = (n + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(silkern::sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, silkern::count_mismatches_kernel, a, b, n, mismatches);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -static_cast<int>(err);
+  }
+  return SILKERN_OK;
+}
+
+extern "C" const char* silkern_status_string_v1(int code) {
+  switch (code) {
+    case SILKERN_OK: return "ok";
+    case SILKERN_E_NULL: return "a required buffer pointer is NULL";
+    case SILKERN_E_SHAPE: return "batch, width or block-table dimensions are out of range";
+    case SILKERN_E_DCP: return "invalid dcp configuration";
+    case SILKERN_E_BLOCK_SIZE: return "block_size must be a positive integer divisible by dcp_interleave";
+    case SILKERN_E_TILE: return "unsupported tile_size";
+    case SILKERN_E_ALIAS: return "an output buffer overlaps an input or another output";
+    case SILKERN_E_GEOMETRY: return "explicit launch geometry rejected";
+    default: break;
+  }
+  if (code < 0) return cudaGetErrorString(static_cast<cudaError_t>(-code));
+  return "unknown status";
+}
+
+extern "C" int silkern_abi_version_v1(void) { return SILKERN_ABI_VERSION; }
+
+extern "C" int64_t silkern_fastdiv_selftest_v1(uint32_t divisor, uint32_t n_begin, uint32_t n_count) {
+  if (divisor == 0 || divisor > (1u << 31)) return -1;
+  const silkern::FastDiv d = silkern::make_fastdiv(divisor);
+  int64_t bad = 0;
+  for (uint64_t k = 0; k < n_count; ++k) {
+    const uint64_t n64 = static_cast<uint64_t>(n_begin) + k;
+    if (n64 >= (uint64_t{1} << 31)) break;
+    const uint32_t n = static_cast<uint32_t>(n64);
+    if (silkern::fastdiv(n, d) != n / divisor) ++bad;
+  }
+  return bad;
+}

@@ -1,0 +1,51 @@
+// Thin inline-PTX wrappers for the sm_90+/sm_100a features the converter uses:
+// programmatic dependent launch, thread-block cluster barriers, distributed
+// shared memory stores and the bulk L2 prefetch.
+#pragma once
+
+#include <cstdint>
+
+namespace silkern {
+
+// Programmatic dependent launch: block until the previous grid in the stream
+// has completed and its memory is visible (no-op when launched without PDL).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Allow the next grid in the stream to start launching its CTAs.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Cluster barrier phases. Every thread of every CTA in the cluster executes
+// each arrive and each wait exactly once, in the same order (".aligned").
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Store v into the copy of `local` that lives in CTA `rank` of this cluster.
+__device__ __forceinline__ void st_shared_cluster(int32_t* local, uint32_t rank, int32_t v) {
+  const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(local));
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(remote), "r"(v) : "memory");
+}
+
+// Hint: bring [ptr, ptr + bytes) into L2. ptr 16-byte aligned, bytes a
+// multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* ptr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+}  // namespace silkern

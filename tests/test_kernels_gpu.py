@@ -1,0 +1,485 @@
+"""Parity of the sm_100a kernels with the reference, through the public API and the C ABI.
+
+Bit-exact (set, count and order) against:
+* every golden case recorded from the reference's own ``localize_reference``
+  and Triton kernels (tests/golden/golden.json), both arms;
+* the C oracle on seeded inputs, over the launch-geometry space (cluster
+  sizes, table staging, L2 prefetch, power-of-two and general arithmetic,
+  misaligned rows) and at the full benchmark sizes.
+Test names and cases follow the reference's tests/test_kernels_gpu.py.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import oracle  # noqa: E402
+from conftest import golden_inputs, input_sha, load_golden  # noqa: E402
+from silkern_b200 import (  # noqa: E402
+    LocalizationError,
+    localize_hierarchical,
+    localize_reference,
+    localize_rowwise,
+    workspace_shapes,
+)
+from silkern_b200.kernels import localize_explicit  # noqa: E402
+from silkern_b200.verify import _random_case  # noqa: E402
+from silkern_b200.workloads import config_case, digest  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("CUDA is required", allow_module_level=True)
+
+DEV = "cuda"
+
+
+def _cuda(values):
+    return torch.as_tensor(np.asarray(values, dtype=np.int32)).to(DEV)
+
+
+def run_rowwise(req, table, tokens, **kw):
+    req, table, tokens = (_cuda(a) for a in (req, table, tokens))
+    out = torch.empty_like(tokens)
+    counts = torch.empty(tokens.shape[0], dtype=torch.int32, device=DEV)
+    localize_rowwise(req, table, tokens, out, counts, **kw)
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), counts.cpu().numpy()
+
+
+def run_hierarchical(req, table, tokens, *, tile_size=128, with_tiles=False, **kw):
+    req, table, tokens = (_cuda(a) for a in (req, table, tokens))
+    batch, width = tokens.shape
+    out = torch.empty_like(tokens)
+    counts = torch.empty(batch, dtype=torch.int32, device=DEV)
+    ws = {name: torch.empty(shape, dtype=torch.int32, device=DEV)
+          for name, shape in workspace_shapes(batch, width, tile_size=tile_size).items()}
+    localize_hierarchical(req, table, tokens, out, counts, ws["mapped"], ws["local_positions"],
+                          ws["tile_counts"], ws["tile_offsets"], tile_size=tile_size, **kw)
+    torch.cuda.synchronize()
+    result = (out.cpu().numpy(), counts.cpu().numpy())
+    if with_tiles:
+        return result + (ws["tile_counts"].cpu().numpy(), ws["tile_offsets"].cpu().numpy())
+    return result
+
+
+def _geometry(entry):
+    return {k: entry[k] for k in ("block_size", "dcp_size", "dcp_rank", "dcp_interleave")}
+
+
+GOLDEN = load_golden()["cases"]
+
+
+@pytest.mark.parametrize("entry", GOLDEN, ids=[c["id"] for c in GOLDEN])
+def test_golden_cases_both_arms(entry) -> None:
+    """Digest-equal to the reference's oracle and Triton kernels on the same inputs."""
+    req, table, tokens = golden_inputs(entry)
+    assert input_sha(req, table, tokens) == entry["input_sha256"]
+    kw = dict(_geometry(entry), compact_valid_to_front=entry["compact_valid_to_front"])
+    assert digest(*run_rowwise(req, table, tokens, **kw)) == entry["oracle_sha256"]
+    tile = entry.get("tile_size", 1024 if entry.get("config") == 4 else 128)
+    out, counts, tc, to = run_hierarchical(req, table, tokens, tile_size=tile, with_tiles=True, **kw)
+    assert digest(out, counts) == entry["oracle_sha256"]
+    if "triton_tiles_sha256" in entry:
+        assert digest(tc, to) == entry["triton_tiles_sha256"]
+    else:
+        want = oracle.tiles(req, table, tokens, tile_size=tile, **_geometry(entry))
+        assert np.array_equal(tc, want[0]) and np.array_equal(to, want[1])
+
+
+def _case(*, width, batch, block_size, dcp_size, seed):
+    return _random_case(width=width, batch=batch, block_size=block_size, dcp_size=dcp_size, seed=seed)
+
+
+@pytest.mark.parametrize("width", [1, 63, 128, 129, 513, 1024, 2048, 4096])
+@pytest.mark.parametrize(("dcp_size", "dcp_rank", "interleave"), [(1, 0, 1), (2, 1, 2), (4, 3, 4), (8, 7, 1)])
+def test_exact_gpu_variants_match_cpu_oracle(width, dcp_size, dcp_rank, interleave) -> None:
+    case = _case(width=width, batch=3, block_size=64, dcp_size=dcp_size,
+                 seed=650000 + width * 31 + dcp_size * 7 + dcp_rank)
+    kw = dict(block_size=64, dcp_size=dcp_size, dcp_rank=dcp_rank, dcp_interleave=interleave)
+    expected = localize_reference(*case, **kw)
+    for arm in (run_rowwise, run_hierarchical):
+        out, counts = arm(*case, **kw)
+        assert out.tolist() == expected[0]
+        assert counts.tolist() == expected[1]
+
+
+def test_exact_gpu_every_rank_and_grouped_interleave() -> None:
+    for dcp_size in (1, 2, 3, 4, 8):
+        case = _case(width=257, batch=4, block_size=48 if dcp_size == 3 else 64, dcp_size=dcp_size,
+                     seed=651000 + dcp_size)
+        for interleave in (1, 2, 4) if dcp_size != 3 else (1, 3):
+            for rank in range(dcp_size):
+                kw = dict(block_size=48 if dcp_size == 3 else 64, dcp_size=dcp_size, dcp_rank=rank,
+                          dcp_interleave=interleave)
+                expected = localize_reference(*case, **kw)
+                for arm in (run_rowwise, run_hierarchical):
+                    out, counts = arm(*case, **kw)
+                    assert out.tolist() == expected[0]
+                    assert counts.tolist() == expected[1]
+
+
+def test_exact_gpu_noncompacting_column_semantics() -> None:
+    case = _case(width=513, batch=3, block_size=32, dcp_size=4, seed=652001)
+    for dcp_size, rank, interleave in ((1, 0, 4), (4, 2, 2), (3, 1, 2)):
+        kw = dict(block_size=32 if dcp_size != 3 else 48, dcp_size=dcp_size, dcp_rank=rank,
+                  dcp_interleave=interleave, compact_valid_to_front=False)
+        expected = localize_reference(*case, **kw)
+        for arm in (run_rowwise, run_hierarchical):
+            out, counts = arm(*case, **kw)
+            assert out.tolist() == expected[0]
+            assert counts.tolist() == expected[1]
+
+
+def _oracle(req, table, tokens, **kw):
+    return oracle.localize(req, table, tokens, threads=4, **kw)
+
+
+def _explicit(req, table, tokens, *, cluster, stage, prefetch, tile_size=0, **kw):
+    req, table, tokens = (_cuda(a) for a in (req, table, tokens))
+    batch, width = tokens.shape
+    out = torch.full_like(tokens, 0x5A5A5A5A)
+    counts = torch.full((batch,), 0x5A5A5A5A, dtype=torch.int32, device=DEV)
+    tc = to = None
+    if tile_size:
+        tiles = (width + tile_size - 1) // tile_size
+        tc = torch.empty((batch, tiles), dtype=torch.int32, device=DEV)
+        to = torch.empty((batch, tiles), dtype=torch.int32, device=DEV)
+    localize_explicit(req, table, tokens, out, counts, cluster_size=cluster, stage_table=stage,
+                      prefetch_table=prefetch, tile_size=tile_size, tile_counts=tc,
+                      tile_offsets=to, **kw)
+    torch.cuda.synchronize()
+    tiles_out = None if tc is None else (tc.cpu().numpy(), to.cpu().numpy())
+    return out.cpu().numpy(), counts.cpu().numpy(), tiles_out
+
+
+def _slices_fit(width, cluster, tile_size):
+    if tile_size:
+        tiles = -(-width // tile_size)
+        per = -(-tiles // cluster)
+        return -(-tiles // per) == cluster
+    slice_ = -(-width // cluster)
+    slice_ = -(-slice_ // 4) * 4
+    return -(-width // slice_) == cluster
+
+
+GEOMETRIES = [
+    # (block_size, dcp_size, dcp_rank, interleave): powers of two, then the general path
+    (64, 4, 1, 1),
+    (64, 8, 7, 2),
+    (48, 3, 2, 3),
+    (40, 5, 0, 1),
+]
+
+
+@pytest.mark.parametrize("width", [1, 3, 5, 63, 64, 127, 129, 257, 513, 1000, 2048, 2049, 4093, 4096,
+                                   8191, 16384])
+@pytest.mark.parametrize("cluster", [1, 2, 4, 8])
+def test_launch_geometry_sweep(width, cluster) -> None:
+    rng = np.random.default_rng(width * 17 + cluster)
+    batch = 3
+    for index, (bs, dcp, rank, il) in enumerate(GEOMETRIES):
+        table_width = int(rng.integers(1, 300))
+        limit = bs * table_width * dcp + 3 * bs * dcp
+        tokens = rng.integers(-4, limit, size=(batch, width), dtype=np.int32)
+        table = rng.integers(-3, 70000, size=(5, table_width), dtype=np.int32)
+        req = rng.integers(0, 5, size=batch, dtype=np.int32)
+        kw = dict(block_size=bs, dcp_size=dcp, dcp_rank=rank, dcp_interleave=il)
+        want = _oracle(req, table, tokens, **kw)
+        stage = index % 2
+        prefetch = (index // 2) % 2
+        for tile_size in (0, 64, 1024):
+            if not _slices_fit(width, cluster, tile_size):
+                continue
+            out, counts, tiles = _explicit(req, table, tokens, cluster=cluster, stage=stage,
+                                           prefetch=prefetch, tile_size=tile_size, **kw)
+            assert np.array_equal(out, want[0]), (kw, tile_size)
+            assert np.array_equal(counts, want[1]), (kw, tile_size)
+            if tile_size:
+                wt = oracle.tiles(req, table, tokens, tile_size=tile_size, **kw)
+                assert np.array_equal(tiles[0], wt[0]) and np.array_equal(tiles[1], wt[1])
+
+
+@pytest.mark.parametrize("stage", [0, 1])
+def test_gather_and_staged_table_agree(stage) -> None:
+    rng = np.random.default_rng(3 + stage)
+    tokens = rng.integers(-2, 600000, size=(17, 2048), dtype=np.int32)
+    table = rng.integers(0, 1 << 20, size=(33, 4096), dtype=np.int32)
+    req = rng.integers(0, 33, size=17, dtype=np.int32)
+    kw = dict(block_size=64, dcp_size=2, dcp_rank=1)
+    want = _oracle(req, table, tokens, **kw)
+    out, counts, _ = _explicit(req, table, tokens, cluster=1, stage=stage, prefetch=1, **kw)
+    assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
+
+
+def test_wide_table_is_gathered() -> None:
+    # table_width above the shared-memory staging limit takes the global gather path
+    rng = np.random.default_rng(9)
+    tokens = rng.integers(0, 64 * 5000 * 2, size=(6, 700), dtype=np.int32)
+    table = rng.integers(0, 1 << 20, size=(3, 5000), dtype=np.int32)
+    req = np.array([2, 0, 1, 1, 0, 2], dtype=np.int32)
+    kw = dict(block_size=64, dcp_size=2, dcp_rank=0)
+    want = _oracle(req, table, tokens, **kw)
+    out, counts = run_rowwise(req, table, tokens, **kw)
+    assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
+    out, counts = run_hierarchical(req, table, tokens, **kw)
+    assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
+
+
+@pytest.mark.parametrize("shift", [(0, 1, 2), (1, 3, 0), (3, 2, 1), (2, 0, 3)])
+@pytest.mark.parametrize("width", [7, 2048, 4096])
+def test_misaligned_views(shift, width) -> None:
+    """Rows whose start is not 16-byte aligned (views into larger storage)."""
+    s_tok, s_out, s_tab = shift
+    rng = np.random.default_rng(width + 10 * s_tok + s_out)
+    batch, twidth = 5, 200
+    tokens_np = rng.integers(-3, 64 * twidth * 4, size=(batch, width), dtype=np.int32)
+    table_np = rng.integers(-2, 90000, size=(6, twidth), dtype=np.int32)
+    req_np = np.array([5, 0, 3, 3, 1], dtype=np.int32)
+    kw = dict(block_size=64, dcp_size=4, dcp_rank=2)
+    want = _oracle(req_np, table_np, tokens_np, **kw)
+
+    def view(values, shift_):
+        backing = torch.zeros(values.size + 8, dtype=torch.int32, device=DEV)
+        v = backing[shift_:shift_ + values.size].view(values.shape)
+        v.copy_(torch.as_tensor(values))
+        return v
+
+    tokens = view(tokens_np, s_tok)
+    table = view(table_np, s_tab)
+    req = view(req_np, 1)
+    out = torch.zeros(batch * width + 8, dtype=torch.int32, device=DEV)[s_out:s_out + batch * width].view(batch, width)
+    counts = torch.zeros(batch + 8, dtype=torch.int32, device=DEV)[3:3 + batch]
+    localize_rowwise(req, table, tokens, out, counts, **kw)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), want[0])
+    assert np.array_equal(counts.cpu().numpy(), want[1])
+    ws = {name: torch.zeros(int(np.prod(shape)) + 4, dtype=torch.int32, device=DEV)[1:1 + int(np.prod(shape))].view(shape)
+          for name, shape in workspace_shapes(batch, width, tile_size=64).items()}
+    out.fill_(7)
+    localize_hierarchical(req, table, tokens, out, counts, ws["mapped"], ws["local_positions"],
+                          ws["tile_counts"], ws["tile_offsets"], tile_size=64, **kw)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), want[0])
+    assert np.array_equal(counts.cpu().numpy(), want[1])
+
+
+def _guarded_cuda(shape, *, guard=32, sentinel=0x5A5A5A5A):
+    elements = int(np.prod(shape))
+    backing = torch.full((elements + 2 * guard,), sentinel, dtype=torch.int32, device=DEV)
+    return backing, backing[guard:guard + elements].view(shape)
+
+
+@pytest.mark.parametrize("arm", ["row_stable", "hierarchical_stable"])
+def test_gpu_canaries_and_input_immutability(arm) -> None:
+    case = _case(width=513, batch=3, block_size=64, dcp_size=4, seed=653001)
+    kw = dict(block_size=64, dcp_size=4, dcp_rank=3, dcp_interleave=4)
+    expected = localize_reference(*case, **kw)
+    guard, sentinel = 32, 0x5A5A5A5A
+    inputs = {}
+
+    def make(name, values):
+        tensor = torch.tensor(values, dtype=torch.int32)
+        backing, view = _guarded_cuda(tuple(tensor.shape), guard=guard, sentinel=sentinel)
+        view.copy_(tensor)
+        inputs[name] = (backing, view.clone())
+        return view
+
+    req, table, tokens = make("req", case[0]), make("table", case[1]), make("tokens", case[2])
+    out_backing, out = _guarded_cuda(tuple(tokens.shape))
+    counts_backing, counts = _guarded_cuda((tokens.shape[0],))
+    guarded_outputs = [out_backing, counts_backing]
+    if arm == "row_stable":
+        localize_rowwise(req, table, tokens, out, counts, **kw)
+    else:
+        ws = {}
+        for name, shape in workspace_shapes(*tokens.shape).items():
+            backing, view = _guarded_cuda(shape)
+            guarded_outputs.append(backing)
+            ws[name] = view
+        localize_hierarchical(req, table, tokens, out, counts, ws["mapped"], ws["local_positions"],
+                              ws["tile_counts"], ws["tile_offsets"], **kw)
+    torch.cuda.synchronize()
+    assert out.cpu().tolist() == expected[0]
+    assert counts.cpu().tolist() == expected[1]
+    for backing, original in inputs.values():
+        n = original.numel()
+        assert torch.all(backing[:guard] == sentinel) and torch.all(backing[guard + n:] == sentinel)
+        assert torch.equal(backing[guard:guard + n].view(original.shape), original)
+    for backing in guarded_outputs:
+        n = backing.numel() - 2 * guard
+        assert torch.all(backing[:guard] == sentinel) and torch.all(backing[guard + n:] == sentinel)
+
+
+def _capture(op):
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            op()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        op()
+    torch.cuda.synchronize()
+    return graph
+
+
+@pytest.mark.parametrize("arm", ["row_stable", "hierarchical_stable"])
+def test_exact_gpu_cuda_graph_replay_and_allocation_stability(arm) -> None:
+    case = _case(width=2048, batch=8, block_size=64, dcp_size=4, seed=654001)
+    kw = dict(block_size=64, dcp_size=4, dcp_rank=2, dcp_interleave=2)
+    expected = localize_reference(*case, **kw)
+    req, table, tokens = (_cuda(v) for v in case)
+    out = torch.empty_like(tokens)
+    counts = torch.empty(tokens.shape[0], dtype=torch.int32, device=DEV)
+    ws = {name: torch.empty(shape, dtype=torch.int32, device=DEV)
+          for name, shape in workspace_shapes(*tokens.shape).items()}
+
+    def op():
+        if arm == "row_stable":
+            localize_rowwise(req, table, tokens, out, counts, **kw)
+        else:
+            localize_hierarchical(req, table, tokens, out, counts, ws["mapped"], ws["local_positions"],
+                                  ws["tile_counts"], ws["tile_offsets"], **kw)
+
+    buffers = (req, table, tokens, out, counts, *ws.values())
+    pointers = [t.data_ptr() for t in buffers]
+    graph = _capture(op)
+    allocated = torch.cuda.memory_allocated()
+    out.fill_(0)
+    for _ in range(100):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() == allocated
+    assert [t.data_ptr() for t in buffers] == pointers
+    assert out.cpu().tolist() == expected[0]
+    assert counts.cpu().tolist() == expected[1]
+
+
+def test_hierarchical_gpu_rejects_workspace_shape_and_alias() -> None:
+    req, table, tokens = _cuda([0]), _cuda([[0, 1]]), _cuda([[0] * 129])
+    out = torch.empty_like(tokens)
+    counts = torch.empty(1, dtype=torch.int32, device=DEV)
+    ws = {name: torch.empty(shape, dtype=torch.int32, device=DEV)
+          for name, shape in workspace_shapes(1, 129).items()}
+    with pytest.raises(LocalizationError, match="tile_counts workspace shape"):
+        localize_hierarchical(req, table, tokens, out, counts, ws["mapped"], ws["local_positions"],
+                              torch.empty((1, 1), dtype=torch.int32, device=DEV), ws["tile_offsets"],
+                              block_size=64, dcp_size=2, dcp_rank=0)
+    with pytest.raises(LocalizationError, match="distinct storage"):
+        localize_hierarchical(req, table, tokens, out, counts, out, ws["local_positions"],
+                              ws["tile_counts"], ws["tile_offsets"], block_size=64, dcp_size=2,
+                              dcp_rank=0)
+
+
+def test_rowwise_rejections() -> None:
+    req, table, tokens = _cuda([0]), _cuda([[0, 1]]), _cuda([[0] * 16])
+    out = torch.empty_like(tokens)
+    counts = torch.empty(1, dtype=torch.int32, device=DEV)
+    kw = dict(block_size=64, dcp_size=2, dcp_rank=0)
+    with pytest.raises(LocalizationError, match="share storage"):
+        localize_rowwise(req, table, tokens, tokens, counts, **kw)
+    with pytest.raises(LocalizationError, match="int32"):
+        localize_rowwise(req, table, tokens.long(), out, counts, **kw)
+    with pytest.raises(LocalizationError, match="contiguous"):
+        localize_rowwise(req, table, _cuda([[0] * 32])[:, ::2], out, counts, **kw)
+    with pytest.raises(LocalizationError, match="CUDA"):
+        localize_rowwise(req.cpu(), table, tokens, out, counts, **kw)
+    with pytest.raises(LocalizationError, match="row width"):
+        wide = torch.zeros((1, 16385), dtype=torch.int32, device=DEV)
+        localize_rowwise(req, table, wide, torch.empty_like(wide), counts, **kw)
+    with pytest.raises(LocalizationError, match="num_warps"):
+        localize_rowwise(req, table, tokens, out, counts, num_warps=2, **kw)
+    with pytest.raises(LocalizationError, match="dcp"):
+        localize_rowwise(req, table, tokens, out, counts, block_size=64, dcp_size=2, dcp_rank=2)
+
+
+def test_out_of_range_request_is_reported_not_read() -> None:
+    rng = np.random.default_rng(1)
+    tokens = rng.integers(0, 64 * 16 * 2, size=(4, 300), dtype=np.int32)
+    table = rng.integers(0, 1000, size=(3, 16), dtype=np.int32)
+    req = np.array([0, 7, 2, -1], dtype=np.int32)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = torch.empty((4, 300), dtype=torch.int32, device=DEV)
+    counts = torch.empty(4, dtype=torch.int32, device=DEV)
+    kw = dict(block_size=64, dcp_size=2, dcp_rank=1)
+    localize_rowwise(_cuda(req), _cuda(table), _cuda(tokens), out, counts, status=status, **kw)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 1
+    got_out, got_counts = out.cpu().numpy(), counts.cpu().numpy()
+    good = np.array([0, 2])
+    want = _oracle(req[good], table, tokens[good], **kw)
+    assert np.array_equal(got_out[good], want[0]) and np.array_equal(got_counts[good], want[1])
+    assert np.all(got_out[[1, 3]] == -1) and np.all(got_counts[[1, 3]] == 0)
+    # a clean call leaves the status word untouched
+    status.zero_()
+    localize_rowwise(_cuda(req[good]), _cuda(table), _cuda(tokens[good]), out[:2], counts[:2],
+                     status=status, **kw)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+
+
+def test_repeated_launches_are_bytewise_identical() -> None:
+    case = config_case(3, seed=31)
+    req, table, tokens = (_cuda(a) for a in (case.req_ids, case.block_table, case.tokens))
+    out = torch.empty_like(tokens)
+    counts = torch.empty(case.batch, dtype=torch.int32, device=DEV)
+    localize_rowwise(req, table, tokens, out, counts, **case.geometry())
+    first = out.clone()
+    for _ in range(20):
+        out.fill_(0)
+        localize_rowwise(req, table, tokens, out, counts, **case.geometry())
+        assert torch.equal(out, first)
+
+
+@pytest.mark.parametrize("config", [2, 3, 4])
+def test_full_size_configs_match_oracle(config) -> None:
+    """Full benchmark sizes: bit-exact against the oracle, every DCP rank."""
+    ranks = {2: 2, 3: 4, 4: 8}[config]
+    total_valid = 0
+    for rank in range(ranks):
+        case = config_case(config, seed=config, dcp_rank=rank)
+        kw = case.geometry()
+        want = _oracle(case.req_ids, case.block_table, case.tokens, **kw)
+        row = run_rowwise(case.req_ids, case.block_table, case.tokens, **kw)
+        hier = run_hierarchical(case.req_ids, case.block_table, case.tokens, tile_size=case.tile_size, **kw)
+        for got in (row, hier):
+            assert np.array_equal(got[0], want[0]) and np.array_equal(got[1], want[1])
+        total_valid += int(want[1].sum())
+    # Every non-negative token belongs to exactly one rank, and the tables cover each
+    # request's context, so the ranks' counts add up to the number of real tokens.
+    assert total_valid == int((config_case(config, seed=config).tokens >= 0).sum())
+
+
+def test_decode_step_of_48_layers_in_one_graph(golden) -> None:
+    """Config 5: 48 converter calls captured in one graph; each layer digest-equal to the reference."""
+    layers = [config_case(5, seed=5000 + layer, dcp_rank=7) for layer in range(48)]
+    expected = {c["seed"]: c["oracle_sha256"] for c in golden["cases"]
+                if c["kind"] == "config" and c["config"] == 5 and c["dcp_rank"] == 7
+                and c["batch_limit"] is None}
+    bufs = []
+    for case in layers:
+        req, table, tokens = (_cuda(a) for a in (case.req_ids, case.block_table, case.tokens))
+        bufs.append((req, table, tokens, torch.empty_like(tokens),
+                     torch.empty(case.batch, dtype=torch.int32, device=DEV)))
+
+    def step():
+        for (req, table, tokens, out, counts), case in zip(bufs, layers, strict=True):
+            localize_rowwise(req, table, tokens, out, counts, **case.geometry())
+
+    graph = _capture(step)
+    allocated = torch.cuda.memory_allocated()
+    for *_, out, counts in bufs:
+        out.fill_(0)
+        counts.fill_(0)
+    for _ in range(10):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() == allocated
+    for (*_, out, counts), layer in zip(bufs, range(48), strict=True):
+        assert digest(out.cpu().numpy(), counts.cpu().numpy()) == expected[5000 + layer]

@@ -1,0 +1,155 @@
+"""The C-ABI library without a GPU: loads, exports every declared symbol, host checks.
+
+No test here launches a kernel. Argument validation happens on the host
+before any CUDA call, so rejected calls are checked with fake addresses that
+are never dereferenced.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from silkern_b200 import _native, workspace_shapes
+from silkern_b200.build import build
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "silkern_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _native.load()
+
+
+def declared_symbols() -> set[str]:
+    text = open(HEADER).read()
+    return set(re.findall(r"\b(silkern_\w+_v1)\s*\(", text))
+
+
+def test_every_declared_symbol_is_exported(lib) -> None:
+    symbols = declared_symbols()
+    assert len(symbols) >= 8
+    assert symbols == set(_native.SIGNATURES)
+    for name in symbols:
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_status_strings(lib) -> None:
+    assert lib.silkern_abi_version_v1() == _native.ABI_VERSION
+    assert _native.status_string(0) == "ok"
+    for code in range(1, 8):
+        assert _native.status_string(code) != "unknown status"
+    assert "dcp" in _native.status_string(3)
+
+
+@pytest.mark.parametrize("width", [1, 129, 2048, 16384])
+@pytest.mark.parametrize("tile", [64, 128, 256, 512, 1024])
+def test_workspace_shapes_abi_matches_python(lib, width, tile) -> None:
+    shapes = (ctypes.c_int64 * 8)()
+    assert lib.silkern_workspace_shapes_v1(5, width, tile, shapes) == 0
+    py = workspace_shapes(5, width, tile_size=tile)
+    flat = [d for key in ("mapped", "local_positions", "tile_counts", "tile_offsets") for d in py[key]]
+    assert list(shapes) == flat
+
+
+def test_workspace_shapes_abi_rejects(lib) -> None:
+    shapes = (ctypes.c_int64 * 8)()
+    assert lib.silkern_workspace_shapes_v1(0, 8, 128, shapes) == 2
+    assert lib.silkern_workspace_shapes_v1(1, 16385, 128, shapes) == 2
+    assert lib.silkern_workspace_shapes_v1(1, 8, 96, shapes) == 5
+    assert lib.silkern_workspace_shapes_v1(1, 8, 2048, shapes) == 5
+
+
+@pytest.mark.parametrize("divisor", [1, 2, 3, 7, 48, 64, 1000, 65537, 2**31 - 1, 2**31])
+def test_fastdiv_sampled_ranges(lib, divisor) -> None:
+    for start in (0, 2**31 - 2**20, 123456789, 2**20):
+        assert lib.silkern_fastdiv_selftest_v1(divisor, start, 2**20) == 0
+
+
+@pytest.mark.parametrize("divisor", [3, 6, 641])
+def test_fastdiv_exhaustive(lib, divisor) -> None:
+    # every numerator the kernels can see (0 .. 2^31 - 1)
+    assert lib.silkern_fastdiv_selftest_v1(divisor, 0, 2**31) == 0
+
+
+def test_fastdiv_random_divisors(lib) -> None:
+    rng = np.random.default_rng(11)
+    for divisor in rng.integers(1, 2**31, size=300):
+        start = int(rng.integers(0, 2**31 - 4096))
+        assert lib.silkern_fastdiv_selftest_v1(int(divisor), start, 4096) == 0
+
+
+# Fake, never-dereferenced device addresses for host-side validation.
+REQ, TABLE, TOK, OUT, CNT = 0x10000, 0x20000, 0x40000, 0x80000, 0xC0000
+
+
+def rowwise(lib, **over):
+    args = dict(req=REQ, table=TABLE, rows=4, twidth=8, tok=TOK, out=OUT, cnt=CNT, batch=4, width=16,
+                bs=64, dcp=2, rank=0, il=1, compact=1)
+    args.update(over)
+    return lib.silkern_localize_rowwise_v1(
+        args["req"], args["table"], args["rows"], args["twidth"], args["tok"], args["out"],
+        args["cnt"], args["batch"], args["width"], args["bs"], args["dcp"], args["rank"],
+        args["il"], args["compact"], None, None,
+    )
+
+
+@pytest.mark.parametrize(
+    ("override", "code"),
+    [
+        ({"req": None}, 1),
+        ({"out": None}, 1),
+        ({"batch": 0}, 2),
+        ({"width": 0}, 2),
+        ({"width": 16385}, 2),
+        ({"rows": 0}, 2),
+        ({"twidth": 0}, 2),
+        ({"dcp": 0}, 3),
+        ({"rank": 2}, 3),
+        ({"rank": -1}, 3),
+        ({"il": 0}, 3),
+        ({"bs": 0}, 4),
+        ({"il": 3}, 4),
+        ({"out": TOK}, 6),
+        ({"out": TOK + 60}, 6),
+        ({"cnt": REQ}, 6),
+        ({"cnt": OUT + 8}, 6),
+    ],
+)
+def test_rowwise_rejects_before_launch(lib, override, code) -> None:
+    assert rowwise(lib, **override) == code
+
+
+def test_hierarchical_rejects_before_launch(lib) -> None:
+    def call(tile, tc=0xD0000, to=0xE0000):
+        return lib.silkern_localize_hierarchical_v1(
+            REQ, TABLE, 4, 8, TOK, OUT, CNT, None, None, tc, to, 4, 16, 64, 2, 0, 1, 1, tile,
+            None, None,
+        )
+
+    assert call(0) == 5
+    assert call(96) == 5
+    assert call(2048) == 5
+    assert call(128, tc=None) == 1
+    assert call(128, tc=OUT) == 6
+    assert call(128, to=0xD0000) == 6
+
+
+def test_explicit_rejects_bad_geometry(lib) -> None:
+    def call(cluster, stage=-1, prefetch=-1, width=16):
+        return lib.silkern_localize_explicit_v1(
+            REQ, TABLE, 4, 8, TOK, OUT, CNT, None, None, 4, width, 64, 2, 0, 1, 1, 0, cluster,
+            stage, prefetch, None, None,
+        )
+
+    assert call(0) == 7
+    assert call(9) == 7
+    assert call(1, stage=2) == 7
+    assert call(1, prefetch=-2) == 7
+    assert call(8, width=16) == 7  # 8 CTAs cannot each own 4-column slices of 16 columns
