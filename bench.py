@@ -385,22 +385,26 @@ def run_e2e(args, case, dev, geometry, dist) -> dict:
     host_in[n_req + n_table:] = torch.as_tensor(case.tokens.ravel())
     lanes = []
     for _ in range(2):
+        # Inputs share one device buffer (one H2D copy); the two outputs must
+        # not share storage, so they come back in two D2H copies.
         dev_in = torch.empty(n_in, dtype=torch.int32, device=dev)
-        dev_out = torch.empty(batch * width + batch, dtype=torch.int32, device=dev)
-        host_out = torch.empty(batch * width + batch, dtype=torch.int32).pin_memory()
+        out = torch.empty((batch, width), dtype=torch.int32, device=dev)
+        counts = torch.empty(batch, dtype=torch.int32, device=dev)
+        host_out = torch.empty((batch, width), dtype=torch.int32).pin_memory()
+        host_counts = torch.empty(batch, dtype=torch.int32).pin_memory()
         req = dev_in[:n_req]
         table = dev_in[n_req:n_req + n_table].view(case.block_table.shape)
         tokens = dev_in[n_req + n_table:].view(batch, width)
-        out = dev_out[: batch * width].view(batch, width)
-        counts = dev_out[batch * width:]
-        lanes.append((torch.cuda.Stream(device=dev), dev_in, dev_out, host_out, req, table, tokens, out, counts))
+        lanes.append((torch.cuda.Stream(device=dev), dev_in, req, table, tokens, out, counts,
+                      host_out, host_counts))
 
     def step(i: int) -> None:
-        stream, dev_in, dev_out, host_out, req, table, tokens, out, counts = lanes[i % 2]
+        stream, dev_in, req, table, tokens, out, counts, host_out, host_counts = lanes[i % 2]
         with torch.cuda.stream(stream):
             dev_in.copy_(host_in, non_blocking=True)
             localize_rowwise(req, table, tokens, out, counts, **geometry)
-            host_out.copy_(dev_out, non_blocking=True)
+            host_out.copy_(out, non_blocking=True)
+            host_counts.copy_(counts, non_blocking=True)
 
     for i in range(max(3, args.warmup)):
         step(i)
