@@ -5,20 +5,26 @@
 // one CTA, and the CTAs of one row form a thread-block cluster (cluster == 1
 // for the common row-wise case). Per CTA:
 //
-//   1. read the row's request id and the slice's tokens with 128-bit loads
-//      (scalar loads only when the slice start is not 16-byte aligned);
-//   2. stage the request's block-table row in shared memory (or gather it
-//      from global memory when the row is wide);
-//   3. apply ownership, deinterleave and paged translation with shifts (all
-//      powers of two) or invariant-divisor multiplies (general case);
-//   4. stable compaction: warp ballots give each lane its prefix inside the
-//      warp, warp totals go through shared memory and a redux.sync per chunk
+//   0. before waiting on the previous grid (programmatic dependent launch),
+//      ask L2 for this slice's tokens, the row's request id and this CTA's
+//      share of the block table. A prefetch only fills L2, which is the
+//      device's point of coherence, so it never returns stale data: loads
+//      issued after the wait see every write of the previous grid. Call
+//      N + 1 therefore reads DRAM while call N is still running;
+//   1. read the request id and the slice's tokens (128-bit loads when the
+//      slice start is 16-byte aligned);
+//   2. apply ownership, deinterleave and paged translation with shifts (all
+//      powers of two) or invariant-divisor multiplies (general case), and
+//      gather the physical block of each valid element from the request's
+//      block-table row (L2-resident after step 0, or staged in shared memory);
+//   3. stable compaction: warp ballots give each lane its prefix inside the
+//      warp, warp totals go through shared memory and one redux.sync per chunk
 //      gives each warp its base; across a cluster, each CTA pushes its total
 //      into every CTA's shared memory (DSMEM) before one cluster barrier.
 //      No atomics, so the order is the selector's order on every run;
-//   5. survivors are staged per warp and written with consecutive stores,
-//      the -1 tail with 128-bit stores; every output element is written
-//      exactly once.
+//   4. each survivor is stored at its final position (a warp's survivors are
+//      one contiguous run), the -1 tail with 128-bit stores; every output
+//      element is written exactly once.
 //
 // Semantics follow silkern/contract.py:67-158 (localize_reference) and the
 // int32 lanes of silkern/kernels.py:51-125 (_rowwise_kernel).
@@ -33,11 +39,13 @@
 
 namespace silkern {
 
-constexpr int kMaxThreads = 1024;
+constexpr int kMaxThreads = 512;
 constexpr int kMaxCluster = 8;
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
-constexpr int kWarpStage = 128;       // survivors one warp stages per chunk (32 lanes x 4)
 constexpr uint32_t kFull = 0xffffffffu;
+constexpr int kModeGeneral = 0;  // invariant-divisor multiplies
+constexpr int kModePow2 = 1;     // interleave, dcp_size, block_size powers of two
+constexpr int kModePow2Il1 = 2;  // ... and interleave 1, single bounds compare
 
 struct Params {
   const int32_t* req_ids;
@@ -49,15 +57,17 @@ struct Params {
   int32_t* tile_offsets;  // hierarchical workspace, or nullptr
   int32_t* status;        // optional error word
   int64_t table_rows;
+  uint64_t table_bytes;   // bytes of the block table covered by the L2 prefetch
+  uint32_t table_chunk;   // per-CTA share of that prefetch (multiple of 16), 0 = off
   uint32_t table_width;
   int32_t width;
-  int32_t slice;          // columns per CTA (multiple of 4, or of tile_size)
+  int32_t slice;          // columns per CTA
   int32_t cluster;        // CTAs per row
-  int32_t stage_entries;  // table entries staged in shared memory (0: gather)
-  int32_t compact;
+  int32_t compact;        // compaction on (selects the kernel instantiation)
   int32_t tile_shift;     // log2(tile_size) when publishing tiles, else -1
   int32_t tiles_per_row;
-  uint32_t prefetch_bytes;  // L2 prefetch: table bytes (multiple of 16), 0 = off
+  int32_t smem_row;       // int offset of the survivor stage in dynamic shared memory
+  int32_t smem_tile;      // int offset of the tile offsets in dynamic shared memory
   uint32_t dcp_rank;
   uint32_t dcp_size;
   uint32_t interleave;
@@ -65,30 +75,9 @@ struct Params {
   // general path
   FastDiv div_il, div_dcp, div_bs;
   // all-powers-of-two path
-  uint32_t il_shift, group_shift, bs_shift;
+  uint32_t il_shift, group_shift, bs_shift, lb_shift;
   uint32_t il_mask, dcp_mask, bs_mask;
 };
-
-// Ownership + deinterleave + logical block of one non-negative token.
-template <bool POW2>
-__device__ __forceinline__ bool locate(uint32_t u, const Params& p, uint32_t& lb, uint32_t& off) {
-  uint32_t owner, local;
-  if constexpr (POW2) {
-    owner = (u >> p.il_shift) & p.dcp_mask;
-    local = ((u >> p.group_shift) << p.il_shift) | (u & p.il_mask);
-    lb = local >> p.bs_shift;
-    off = local & p.bs_mask;
-  } else {
-    const uint32_t q1 = fastdiv(u, p.div_il);   // t / interleave
-    const uint32_t r1 = u - q1 * p.interleave;  // t % interleave
-    const uint32_t q2 = fastdiv(q1, p.div_dcp);  // t / (dcp_size * interleave)
-    owner = q1 - q2 * p.dcp_size;                // (t / interleave) % dcp_size
-    local = q2 * p.interleave + r1;
-    lb = fastdiv(local, p.div_bs);
-    off = local - lb * p.block_size;
-  }
-  return owner == p.dcp_rank && lb < p.table_width;
-}
 
 // out[lo:hi] = -1 with 128-bit stores on the aligned body.
 __device__ __forceinline__ void fill_invalid(int32_t* row, int lo, int hi, int tid, int nthreads) {
@@ -105,9 +94,32 @@ __device__ __forceinline__ void fill_invalid(int32_t* row, int lo, int hi, int t
   if (tid < rest) dst[head + 4 * nvec + tid] = -1;
 }
 
-template <int NC, bool POW2>
+// dst[0:n] = src[0:n] (src in shared memory) with 128-bit stores on the
+// aligned body of dst.
+__device__ __forceinline__ void copy_from_shared(int32_t* dst, const int32_t* src, int n, int tid,
+                                                 int nthreads) {
+  if (n <= 0) return;
+  int head = static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 2);
+  head = head < n ? head : n;
+  if (tid < head) dst[tid] = src[tid];
+  const int nvec = (n - head) >> 2;
+  int4* body = reinterpret_cast<int4*>(dst + head);
+  const int32_t* s = src + head;
+  for (int g = tid; g < nvec; g += nthreads) {
+    body[g] = make_int4(s[4 * g], s[4 * g + 1], s[4 * g + 2], s[4 * g + 3]);
+  }
+  const int rest = n - head - 4 * nvec;
+  if (tid < rest) dst[head + 4 * nvec + tid] = src[head + 4 * nvec + tid];
+}
+
+// NC chunks of four columns per thread; CLUSTER: rows split over a cluster;
+// MODE: general arithmetic, all powers of two, or all powers of two with
+// interleave 1; STAGE: the block-table row is staged in shared memory instead
+// of gathered from L2; COMPACT: valid values go to the front of the row.
+template <int NC, bool CLUSTER, int MODE, bool STAGE, bool COMPACT>
 __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_constant__ Params p) {
-  extern __shared__ __align__(16) int32_t smem[];
+  extern __shared__ __align__(16) int32_t smem[];  // [table stage][survivors][tile offsets]
+  __shared__ int32_t s_wt[NC * 32];                // warp totals per chunk
   __shared__ int32_t s_cta_total[kMaxCluster];
 
   const int nthreads = blockDim.x;
@@ -115,40 +127,40 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int cs = p.cluster;
-  const int64_t row = blockIdx.x / static_cast<uint32_t>(cs);
-  const int crank = static_cast<int>(blockIdx.x - row * cs);
-
-  int32_t* s_tbl = smem;
-  int32_t* s_wt = s_tbl + p.stage_entries;  // [NC][32] warp totals
-  int32_t* s_stage = s_wt + NC * 32;        // [nwarps][kWarpStage]
-  int32_t* s_tile = s_stage + nwarps * kWarpStage;
-
-  if (cs > 1) cluster_arrive_relaxed();  // phase 0: this CTA is resident
-
-  pdl_wait();
-  pdl_launch_dependents();
-
-  if (p.prefetch_bytes != 0 && tid == 0) {
-    // Each CTA warms L2 with its share of the whole block table while the
-    // request id (on which its own table row depends) is still in flight.
-    const uint64_t total = p.prefetch_bytes;
-    const uint64_t nblk = gridDim.x;
-    const uint64_t chunk = (((total + nblk - 1) / nblk) + 15u) & ~uint64_t{15};
-    const uint64_t begin = blockIdx.x * chunk;
-    if (begin < total) {
-      const uint64_t end = begin + chunk < total ? begin + chunk : total;
-      prefetch_l2_bulk(reinterpret_cast<const char*>(p.table) + begin, static_cast<uint32_t>(end - begin));
-    }
+  int64_t row;
+  int crank;
+  if constexpr (CLUSTER) {
+    row = cluster_id_x();
+    crank = static_cast<int>(cluster_ctarank());
+    cluster_arrive_relaxed();  // phase 0: this CTA is resident
+  } else {
+    row = blockIdx.x;
+    crank = 0;
   }
-
-  const int32_t req = __ldg(p.req_ids + row);
+  pdl_launch_dependents();
 
   const int c0 = crank * p.slice;
   const int len = min(p.slice, p.width - c0);
   const int32_t* tok = p.tokens + row * p.width + c0;
-  const bool tok_vec = (reinterpret_cast<uintptr_t>(tok) & 15u) == 0;
 
+  if (tid == 0) {
+    prefetch_l2_line(p.req_ids + row);
+    const uintptr_t lo = (reinterpret_cast<uintptr_t>(tok) + 15u) & ~uintptr_t{15};
+    const uintptr_t hi = reinterpret_cast<uintptr_t>(tok + len) & ~uintptr_t{15};
+    if (hi > lo) prefetch_l2_bulk(reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo));
+    if (p.table_chunk != 0) {
+      const uint64_t begin = static_cast<uint64_t>(blockIdx.x) * p.table_chunk;
+      if (begin < p.table_bytes) {
+        const uint64_t end = begin + p.table_chunk < p.table_bytes ? begin + p.table_chunk : p.table_bytes;
+        prefetch_l2_bulk(reinterpret_cast<const char*>(p.table) + begin, static_cast<uint32_t>(end - begin));
+      }
+    }
+  }
+
+  pdl_wait();  // everything below may read what the previous grid wrote
+
+  const int32_t req = __ldg(p.req_ids + row);
+  const bool tok_vec = (reinterpret_cast<uintptr_t>(tok) & 15u) == 0;
   int32_t val[NC][4];
 #pragma unroll
   for (int i = 0; i < NC; ++i) {
@@ -171,9 +183,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
   }
   const int32_t* trow = p.table + static_cast<int64_t>(req_ok ? req : 0) * p.table_width;
 
-  if (p.stage_entries != 0) {
+  int32_t* s_tbl = smem;
+  if constexpr (STAGE) {
     if (req_ok) {
-      const int n = p.stage_entries;
+      const int n = static_cast<int>(p.table_width);
       if ((reinterpret_cast<uintptr_t>(trow) & 15u) == 0) {
         const int nvec = n >> 2;
         const int4* src = reinterpret_cast<const int4*>(trow);
@@ -187,35 +200,64 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
     __syncthreads();
   }
 
-  // Map every element; val becomes the physical slot (or -1), bits[i] marks
-  // the valid ones.
+  // Map every element in place: val becomes the physical slot or -1, bits[i]
+  // marks the valid ones. A row whose request id is outside the table keeps
+  // no element (table width 0).
+  const uint32_t twidth = req_ok ? p.table_width : 0u;
   uint32_t bits[NC];
-  int lane_pre[NC];
-  int warp_tot[NC];
-  const uint32_t lt = lanemask_lt();
 #pragma unroll
   for (int i = 0; i < NC; ++i) {
     uint32_t b = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int32_t t = val[i][j];
-      int32_t phys = -1;
-      uint32_t lb, off;
-      if (t >= 0 && req_ok && locate<POW2>(static_cast<uint32_t>(t), p, lb, off)) {
-        const int32_t blk = p.stage_entries != 0 ? s_tbl[lb] : __ldg(trow + lb);
-        phys = static_cast<int32_t>(static_cast<uint32_t>(blk) * p.block_size + off);
-        b |= 1u << j;
+      const uint32_t u = static_cast<uint32_t>(t);
+      bool ok;
+      uint32_t lb, local;
+      if constexpr (MODE == kModePow2Il1) {
+        // interleave 1: local = t >> log2(dcp), owner = t & (dcp - 1). The host
+        // checked 2^(31 - lb_shift) >= table_width, so lb < table_width also
+        // rejects negative tokens.
+        local = u >> p.group_shift;
+        lb = u >> p.lb_shift;
+        ok = lb < twidth && (u & p.dcp_mask) == p.dcp_rank;
+      } else if constexpr (MODE == kModePow2) {
+        local = ((u >> p.group_shift) << p.il_shift) | (u & p.il_mask);
+        lb = local >> p.bs_shift;
+        ok = t >= 0 && ((u >> p.il_shift) & p.dcp_mask) == p.dcp_rank && lb < twidth;
+      } else {
+        const uint32_t q1 = fastdiv(u, p.div_il);   // t / interleave
+        const uint32_t q2 = fastdiv(q1, p.div_dcp);  // t / (dcp_size * interleave)
+        local = q2 * p.interleave + (u - q1 * p.interleave);
+        lb = fastdiv(local, p.div_bs);
+        ok = t >= 0 && q1 - q2 * p.dcp_size == p.dcp_rank && lb < twidth;  // owner == rank
+      }
+      // physical = table[lb] * block_size + (local - lb * block_size), one
+      // multiply-add, wrapping like the reference's int32 lanes. Compacting
+      // calls never store an invalid element, so only in-place calls need -1.
+      int32_t phys = COMPACT ? 0 : -1;
+      if (ok) {
+        const int32_t blk = STAGE ? s_tbl[lb] : __ldg(trow + lb);
+        phys = static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * p.block_size + local);
       }
       val[i][j] = phys;
+      b |= ok ? (1u << j) : 0u;
     }
     bits[i] = b;
-    const uint32_t b0 = __ballot_sync(kFull, b & 1u);
-    const uint32_t b1 = __ballot_sync(kFull, b & 2u);
-    const uint32_t b2 = __ballot_sync(kFull, b & 4u);
-    const uint32_t b3 = __ballot_sync(kFull, b & 8u);
-    lane_pre[i] = __popc(b0 & lt) + __popc(b1 & lt) + __popc(b2 & lt) + __popc(b3 & lt);
-    warp_tot[i] = __popc(b0) + __popc(b1) + __popc(b2) + __popc(b3);
-    if (lane == 0) s_wt[i * 32 + warp] = warp_tot[i];
+  }
+
+  // Lane prefix inside the warp from three ballots over the per-lane count
+  // (0..4, three bits), warp totals through shared memory, per chunk.
+  int lane_pre[NC];
+  const uint32_t lt = lanemask_lt();
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const uint32_t c = __popc(bits[i]);
+    const uint32_t b0 = __ballot_sync(kFull, c & 1u);
+    const uint32_t b1 = __ballot_sync(kFull, c & 2u);
+    const uint32_t b2 = __ballot_sync(kFull, c & 4u);
+    lane_pre[i] = __popc(b0 & lt) + 2 * __popc(b1 & lt) + 4 * __popc(b2 & lt);
+    if (lane == 0) s_wt[i * 32 + warp] = __popc(b0) + 2 * __popc(b1) + 4 * __popc(b2);
   }
   __syncthreads();
 
@@ -226,16 +268,15 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
 #pragma unroll
   for (int i = 0; i < NC; ++i) {
     const int x = lane < nwarps ? s_wt[i * 32 + lane] : 0;
-    const int before = __reduce_add_sync(kFull, lane < warp ? x : 0);
-    const int tot = __reduce_add_sync(kFull, x);
-    base[i] = run + before;
-    run += tot;
+    base[i] = run + __reduce_add_sync(kFull, lane < warp ? x : 0);
+    run += __reduce_add_sync(kFull, x);
   }
   const int cta_total = run;
 
   int row_off = 0;
   int row_total = cta_total;
-  if (cs > 1) {
+  if constexpr (CLUSTER) {
+    const int cs = p.cluster;
     cluster_wait_acquire();  // phase 0 complete: every CTA of the cluster runs
     if (tid < cs) st_shared_cluster(&s_cta_total[crank], static_cast<uint32_t>(tid), cta_total);
     cluster_arrive_release();
@@ -249,22 +290,52 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
   }
 
   int32_t* orow = p.out + row * p.width;
-  if (p.compact) {
-    int32_t* stage = s_stage + warp * kWarpStage;
+  if constexpr (COMPACT) {
+    // Stage this CTA's survivors compactly in shared memory, then write them
+    // and the -1 tail with 128-bit stores, each output element once.
+    int32_t* s_row = smem + p.smem_row;
 #pragma unroll
     for (int i = 0; i < NC; ++i) {
-      int pos = lane_pre[i];
+      int32_t* dst = s_row + base[i] + lane_pre[i];
+      int k = 0;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (bits[i] & (1u << j)) stage[pos++] = val[i][j];
+        if (bits[i] & (1u << j)) dst[k] = val[i][j];
+        k += (bits[i] >> j) & 1u;
       }
-      __syncwarp();
-      const int n = warp_tot[i];
-      int32_t* dst = orow + row_off + base[i];
-      for (int e = lane; e < n; e += 32) dst[e] = stage[e];
-      __syncwarp();
     }
-    fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
+    __syncthreads();
+    if constexpr (CLUSTER) {
+      copy_from_shared(orow + row_off, s_row, cta_total, tid, nthreads);
+      fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
+    } else {
+      // The whole row is this CTA's: granule g holds survivors below
+      // cta_total and -1 from there on.
+      const bool out_vec = (reinterpret_cast<uintptr_t>(orow) & 15u) == 0;
+#pragma unroll
+      for (int i = 0; i < NC; ++i) {
+        const int col = 4 * (i * nthreads + tid);
+        if (col < len) {
+          int4 v;
+          if (col + 4 <= cta_total) {
+            v = *reinterpret_cast<const int4*>(s_row + col);
+          } else if (col >= cta_total) {
+            v = make_int4(-1, -1, -1, -1);
+          } else {
+            const int4 q = *reinterpret_cast<const int4*>(s_row + col);
+            v = make_int4(q.x, col + 1 < cta_total ? q.y : -1, col + 2 < cta_total ? q.z : -1, -1);
+          }
+          if (out_vec && col + 4 <= len) {
+            *reinterpret_cast<int4*>(orow + col) = v;
+          } else {
+            orow[col] = v.x;
+            if (col + 1 < len) orow[col + 1] = v.y;
+            if (col + 2 < len) orow[col + 2] = v.z;
+            if (col + 3 < len) orow[col + 3] = v.w;
+          }
+        }
+      }
+    }
   } else {
     int32_t* dst = orow + c0;
     const bool out_vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
@@ -285,6 +356,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
   if (p.tile_shift >= 0) {
     // Publish the tile decomposition: the exclusive position of the element
     // in a tile's first column is that tile's offset; counts are differences.
+    int32_t* s_tile = smem + p.smem_tile;
     const int tmask = (1 << p.tile_shift) - 1;
 #pragma unroll
     for (int i = 0; i < NC; ++i) {
@@ -316,8 +388,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
 __global__ void __launch_bounds__(256) count_mismatches_kernel(const int32_t* a, const int32_t* b,
                                                                int64_t n, int32_t* mismatches) {
   __shared__ int s_part[8];
-  pdl_wait();
   pdl_launch_dependents();
+  pdl_wait();
   int local = 0;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -341,11 +413,38 @@ namespace {
 
 using KernelFn = void (*)(Params);
 
-KernelFn pick_kernel(int nc, bool pow2) {
+template <int NC, bool CLUSTER, int MODE, bool STAGE>
+KernelFn pick_compact(bool compact) {
+  return compact ? localize_kernel<NC, CLUSTER, MODE, STAGE, true>
+                 : localize_kernel<NC, CLUSTER, MODE, STAGE, false>;
+}
+
+template <int NC, bool CLUSTER, int MODE>
+KernelFn pick_stage(bool stage, bool compact) {
+  return stage ? pick_compact<NC, CLUSTER, MODE, true>(compact)
+               : pick_compact<NC, CLUSTER, MODE, false>(compact);
+}
+
+template <int NC, bool CLUSTER>
+KernelFn pick_mode(int mode, bool stage, bool compact) {
+  switch (mode) {
+    case kModePow2Il1: return pick_stage<NC, CLUSTER, kModePow2Il1>(stage, compact);
+    case kModePow2: return pick_stage<NC, CLUSTER, kModePow2>(stage, compact);
+    default: return pick_stage<NC, CLUSTER, kModeGeneral>(stage, compact);
+  }
+}
+
+template <int NC>
+KernelFn pick_for_nc(bool cluster, int mode, bool stage, bool compact) {
+  return cluster ? pick_mode<NC, true>(mode, stage, compact) : pick_mode<NC, false>(mode, stage, compact);
+}
+
+KernelFn pick_kernel(int nc, bool cluster, int mode, bool stage, bool compact) {
   switch (nc) {
-    case 1: return pow2 ? localize_kernel<1, true> : localize_kernel<1, false>;
-    case 2: return pow2 ? localize_kernel<2, true> : localize_kernel<2, false>;
-    case 4: return pow2 ? localize_kernel<4, true> : localize_kernel<4, false>;
+    case 1: return pick_for_nc<1>(cluster, mode, stage, compact);
+    case 2: return pick_for_nc<2>(cluster, mode, stage, compact);
+    case 4: return pick_for_nc<4>(cluster, mode, stage, compact);
+    case 8: return pick_for_nc<8>(cluster, mode, stage, compact);
     default: return nullptr;
   }
 }
@@ -411,7 +510,10 @@ int validate(const Request& r) {
   }
   const int64_t bw = r.batch * r.width;
   const int64_t tiles = r.tile_size ? r.batch * ((r.width + r.tile_size - 1) / r.tile_size) : 0;
-  struct Range { const void* p; int64_t n; };
+  struct Range {
+    const void* p;
+    int64_t n;
+  };
   const Range inputs[3] = {{r.req_ids, r.batch}, {r.table, r.table_rows * r.table_width}, {r.tokens, bw}};
   const Range outputs[4] = {{r.out, bw}, {r.counts, r.batch}, {r.tile_counts, tiles}, {r.tile_offsets, tiles}};
   for (const Range& o : outputs) {
@@ -436,12 +538,14 @@ struct Geometry {
   bool prefetch;
 };
 
-// Chunks per thread and threads per CTA for a slice of `slice` columns.
+// Chunks of four columns per thread and threads per CTA for `slice` columns:
+// up to kMaxThreads threads with one chunk each, then more chunks per thread
+// (short per-thread dependency chains measured faster than fewer, longer ones).
 bool fit_slice(int slice, int* nc, int* threads) {
   const int granules = (slice + 3) / 4;
   int c = 1;
   while (granules > c * kMaxThreads) c *= 2;
-  if (c > 4) return false;
+  if (c > 8) return false;
   int t = (granules + c - 1) / c;
   t = (t + 31) / 32 * 32;
   *nc = c;
@@ -454,13 +558,17 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
   int cs;
   int slice;
   if (r.tile_size != 0) {
-    // Hierarchical: a CTA covers a whole number of tiles, at most 8 CTAs/row.
+    // Hierarchical: a CTA covers a whole number of tiles, at most 8 CTAs per
+    // row, and (unless the row is shorter) at least 1024 columns.
     const int tiles = (width + r.tile_size - 1) / r.tile_size;
     int per_cta;
     if (cluster_req > 0) {
       per_cta = (tiles + cluster_req - 1) / cluster_req;
     } else {
       per_cta = (tiles + kMaxCluster - 1) / kMaxCluster;
+      const int min_tiles = (1024 + r.tile_size - 1) / r.tile_size;
+      if (per_cta < min_tiles) per_cta = min_tiles;
+      if (per_cta > tiles) per_cta = tiles;
     }
     slice = per_cta * r.tile_size;
     cs = (tiles + per_cta - 1) / per_cta;
@@ -472,7 +580,7 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
       // few rows to occupy the SMs.
       const int sms = sm_count();
       cs = 1;
-      while (cs < kMaxCluster && r.batch * cs < sms && width / (2 * cs) >= 1024) cs *= 2;
+      while (cs < kMaxCluster && r.batch * cs * 2 <= sms && width / (2 * cs) >= 1024) cs *= 2;
     }
     slice = (width + cs - 1) / cs;
     slice = (slice + 3) / 4 * 4;
@@ -484,15 +592,24 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
   g->cluster = cs;
   g->slice = slice;
   if (stage_req == 1 && r.table_width > kTableStageMax) return SILKERN_E_GEOMETRY;
-  g->stage = stage_req >= 0 ? stage_req == 1 : r.table_width <= kTableStageMax;
+  g->stage = stage_req == 1;
   const int64_t table_bytes = r.table_rows * r.table_width * 4;
   const bool aligned = (reinterpret_cast<uintptr_t>(r.table) & 15u) == 0;
-  bool prefetch = aligned && table_bytes >= 16 && table_bytes <= 2 * r.batch * r.width * 4 &&
-                  table_bytes <= (int64_t{1} << 31);
-  if (prefetch_req >= 0) prefetch = prefetch_req == 1 && aligned && table_bytes >= 16 &&
-                                    table_bytes <= (int64_t{1} << 31);
-  g->prefetch = prefetch;
+  const bool possible = aligned && table_bytes >= 16 && table_bytes <= (int64_t{1} << 32);
+  g->prefetch = prefetch_req >= 0 ? (prefetch_req == 1 && possible)
+                                   : (possible && table_bytes <= 2 * r.batch * r.width * 4);
   if (r.batch * cs > INT32_MAX) return SILKERN_E_SHAPE;
+  return SILKERN_OK;
+}
+
+// Dynamic shared memory above 48 KB must be enabled per kernel and device.
+int allow_large_smem(KernelFn fn, size_t bytes) {
+  const cudaError_t err =
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -static_cast<int>(err);
+  }
   return SILKERN_OK;
 }
 
@@ -517,12 +634,18 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req) {
   p.width = static_cast<int32_t>(r.width);
   p.slice = g.slice;
   p.cluster = g.cluster;
-  p.stage_entries = g.stage ? static_cast<int32_t>(r.table_width) : 0;
   p.compact = (r.compact_flag != 0 && r.dcp_size > 1) ? 1 : 0;
   p.tile_shift = r.tile_size ? static_cast<int32_t>(log2_exact(static_cast<uint32_t>(r.tile_size))) : -1;
   p.tiles_per_row = r.tile_size ? static_cast<int32_t>((r.width + r.tile_size - 1) / r.tile_size) : 0;
-  const int64_t table_bytes = r.table_rows * r.table_width * 4;
-  p.prefetch_bytes = g.prefetch ? static_cast<uint32_t>(table_bytes & ~int64_t{15}) : 0u;
+  const int64_t grid = r.batch * g.cluster;
+  if (g.prefetch) {
+    const uint64_t bytes = static_cast<uint64_t>(r.table_rows * r.table_width * 4) & ~uint64_t{15};
+    uint64_t chunk = (bytes + static_cast<uint64_t>(grid) - 1) / static_cast<uint64_t>(grid);
+    chunk = (chunk + 15u) & ~uint64_t{15};
+    if (chunk < 256) chunk = 256;
+    p.table_bytes = bytes;
+    p.table_chunk = static_cast<uint32_t>(chunk);
+  }
   p.dcp_rank = static_cast<uint32_t>(r.dcp_rank);
   p.dcp_size = static_cast<uint32_t>(r.dcp_size);
   p.interleave = static_cast<uint32_t>(r.interleave);
@@ -532,24 +655,40 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req) {
   p.div_bs = make_fastdiv(p.block_size);
   const bool pow2 = is_pow2(p.interleave) && is_pow2(p.dcp_size) && is_pow2(p.block_size) &&
                     log2_exact(p.interleave) + log2_exact(p.dcp_size) <= 31;
+  int mode = kModeGeneral;
   if (pow2) {
     p.il_shift = log2_exact(p.interleave);
     p.group_shift = p.il_shift + log2_exact(p.dcp_size);
     p.bs_shift = log2_exact(p.block_size);
+    p.lb_shift = p.group_shift + p.bs_shift;
     p.il_mask = p.interleave - 1;
     p.dcp_mask = p.dcp_size - 1;
     p.bs_mask = p.block_size - 1;
+    mode = kModePow2;
+    // interleave 1 and a table no wider than 2^(31 - lb_shift): one unsigned
+    // compare of t >> lb_shift against the width rejects negative tokens too.
+    if (p.interleave == 1 && p.lb_shift <= 30 &&
+        static_cast<uint64_t>(p.table_width) <= (uint64_t{1} << (31 - p.lb_shift))) {
+      mode = kModePow2Il1;
+    }
   }
 
-  KernelFn fn = pick_kernel(g.nc, pow2);
+  KernelFn fn = pick_kernel(g.nc, g.cluster > 1, mode, g.stage, p.compact != 0);
   if (fn == nullptr) return SILKERN_E_GEOMETRY;
-  const int nwarps = g.threads / 32;
   const int ntiles_cta = r.tile_size ? (g.slice + r.tile_size - 1) / r.tile_size : 0;
-  const size_t smem = sizeof(int32_t) * (static_cast<size_t>(p.stage_entries) + g.nc * 32 +
-                                         static_cast<size_t>(nwarps) * kWarpStage + ntiles_cta);
+  // dynamic shared memory: [table stage][survivor stage (16-byte aligned)][tile offsets]
+  const int stage_ints = g.stage ? static_cast<int>((r.table_width + 3) / 4 * 4) : 0;
+  const int row_ints = p.compact ? (g.slice + 3) / 4 * 4 : 0;
+  p.smem_row = stage_ints;
+  p.smem_tile = stage_ints + row_ints;
+  const size_t smem = sizeof(int32_t) * static_cast<size_t>(stage_ints + row_ints + ntiles_cta);
+  if (smem > 48 * 1024) {
+    rc = allow_large_smem(fn, smem);
+    if (rc != SILKERN_OK) return rc;
+  }
 
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(r.batch * g.cluster), 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
   cfg.blockDim = dim3(static_cast<unsigned>(g.threads), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = r.stream;

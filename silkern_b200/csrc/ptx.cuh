@@ -42,6 +42,23 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* ptr, uint32_t bytes
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
 }
 
+// Hint: bring the 128-byte line holding ptr into L2.
+__device__ __forceinline__ void prefetch_l2_line(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr) : "memory");
+}
+
+// Index of this cluster in the grid (x) and of this CTA inside its cluster.
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t v;
+  asm("mov.u32 %0, %%clusterid.x;" : "=r"(v));
+  return v;
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t v;
+  asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(v));
+  return v;
+}
+
 __device__ __forceinline__ uint32_t lanemask_lt() {
   uint32_t m;
   asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
