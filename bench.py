@@ -171,6 +171,28 @@ def _cpu_baseline(threads: int, seconds: float = 2.0) -> dict:
     }
 
 
+def shard_plan(rank: int, world: int) -> dict:
+    """What one rank converts: its DCP rank and the seed of its own inputs.
+
+    Ranks are independent shards (no data is exchanged); rank r converts the
+    DCP rank r % 4 on inputs seeded by its global rank.
+    """
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    return {"dcp_rank": rank % DCP_SIZE, "base_seed": 1000 * (rank + 1)}
+
+
+def reduce_max(dist, value: float) -> float:
+    """Max of a host float over all ranks (gloo), or the value itself without dist."""
+    if dist is None:
+        return float(value)
+    import torch
+
+    t = torch.tensor([float(value)], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def _host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -234,8 +256,9 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    dcp_rank = rank % DCP_SIZE
-    base_seed = 1000 * (rank + 1)
+    plan = shard_plan(rank, world)
+    dcp_rank = plan["dcp_rank"]
+    base_seed = plan["base_seed"]
 
     # Distinct seeded cases, laid out in BUFFER_SETS separate resident buffer sets.
     cases = [config_case(CONFIG, seed=base_seed + i, dcp_rank=dcp_rank) for i in range(DISTINCT_CASES)]
@@ -303,11 +326,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
         torch.cuda.synchronize(dev)
     if dist is not None:
         dist.barrier()
-    elapsed_ms = start.elapsed_time(end)
-    if dist is not None:
-        t = torch.tensor([elapsed_ms], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
+    elapsed_ms = reduce_max(dist, start.elapsed_time(end))
     per_call_s = elapsed_ms / 1e3 / args.steps
 
     # The timed outputs must be the reference's: check every buffer set.
@@ -424,12 +443,9 @@ def run_e2e(args, case, dev, geometry, dist) -> dict:
         current.wait_stream(lane[0])
     end.record(current)
     torch.cuda.synchronize(dev)
-    elapsed_ms = start.elapsed_time(end)
     if dist is not None:
         dist.barrier()
-        t = torch.tensor([elapsed_ms], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
+    elapsed_ms = reduce_max(dist, start.elapsed_time(end))
     world = dist.get_world_size() if dist is not None else 1
     per_step = elapsed_ms / 1e3 / steps
     return {

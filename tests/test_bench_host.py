@@ -1,0 +1,90 @@
+"""Host-side logic of the multi-GPU bench, on CPU: gloo ranks, no GPU.
+
+Each rank of ``bench.py`` converts its own DCP rank independently; the only
+cross-process steps are a barrier and a max-reduction of the timed duration.
+Here two gloo processes run exactly those steps.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+import bench
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_shard_plan_assigns_every_dcp_rank_and_distinct_seeds() -> None:
+    plans = [bench.shard_plan(r, 8) for r in range(8)]
+    assert [p["dcp_rank"] for p in plans] == [0, 1, 2, 3, 0, 1, 2, 3]
+    assert len({p["base_seed"] for p in plans}) == 8
+    with pytest.raises(ValueError):
+        bench.shard_plan(2, 2)
+
+
+def test_reduce_max_without_dist() -> None:
+    assert bench.reduce_max(None, 1.5) == 1.5
+
+
+def _worker(rank: int, world: int, port: int, out_path: str) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        plan = bench.shard_plan(rank, world)
+        dist.barrier()
+        value = bench.reduce_max(dist, 10.0 * (rank + 1))
+        with open(f"{out_path}.{rank}", "w") as fh:
+            json.dump({"plan": plan, "max": value}, fh)
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_two_gloo_ranks_barrier_and_max(tmp_path) -> None:
+    import torch.multiprocessing as mp
+
+    port = _free_port()
+    out = str(tmp_path / "rank")
+    mp.start_processes(_worker, args=(2, port, out), nprocs=2, join=True, start_method="spawn")
+    results = [json.load(open(f"{out}.{r}")) for r in range(2)]
+    assert [r["plan"]["dcp_rank"] for r in results] == [0, 1]
+    assert all(r["max"] == 20.0 for r in results)
+
+
+def test_reference_arm_line_on_cpu() -> None:
+    proc = subprocess.run(
+        [sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "2",
+         "--warmup", "1"],
+        capture_output=True, text=True, timeout=300, check=True,
+    )
+    line = json.loads(proc.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference"
+    assert line["unit"] == "Gindices/s" and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port"
+    assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_reference_arm_other_ranks_print_nothing() -> None:
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2")
+    proc = subprocess.run(
+        [sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "1",
+         "--warmup", "0"],
+        capture_output=True, text=True, timeout=300, check=True, env=env,
+    )
+    assert proc.stdout.strip() == ""
