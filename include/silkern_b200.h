@@ -49,6 +49,7 @@ extern "C" {
 #define SILKERN_E_TILE 5         /* unsupported tile_size */
 #define SILKERN_E_ALIAS 6        /* an output overlaps an input or another output */
 #define SILKERN_E_GEOMETRY 7     /* explicit launch geometry rejected */
+#define SILKERN_E_SCRATCH 8      /* batch x tiles exceeds SILKERN_NOALLOC_MAX_TILES */
 
 #define SILKERN_STATUS_BAD_REQUEST 1
 
@@ -125,6 +126,38 @@ int silkern_localize_explicit_v1(const int32_t* req_ids, const int32_t* block_ta
                                  int32_t compact_valid_to_front, int32_t tile_size,
                                  int32_t cluster_size, int32_t stage_table,
                                  int32_t prefetch_table, int32_t* status, void* stream);
+
+/*
+ * Hierarchical localization for callers that cannot allocate device memory:
+ * the same computation and outputs (out, counts) as
+ * silkern_localize_hierarchical_v1, but without workspace arguments. Its
+ * tile workspace (tile counts and tile offsets) lives in a fixed array inside
+ * this library, SILKERN_NOALLOC_MAX_TILES entries for each, 256 KiB in total,
+ * which every GPU that loads the library holds until the process exits.
+ * Callers whose memory is planned outside their control use it: plugin hosts
+ * and serving runtimes whose enqueue path forbids cudaMalloc, or code run
+ * while another framework records a CUDA graph, where a new allocation would
+ * break the recording or stall it.
+ *   - batch * ceil(width / tile_size) above SILKERN_NOALLOC_MAX_TILES is
+ *     rejected with SILKERN_E_SCRATCH before anything is launched;
+ *   - the first call on a device looks up the array's device address with
+ *     that device current, so make that first call before any stream capture;
+ *   - every call shares the one array and leaves its tile decomposition there
+ *     (nothing in it has to start at zero: each call writes every entry it
+ *     uses before reading any), so calls that overlap on the GPU, from two
+ *     streams or two threads, race on it and must be serialised.
+ * Nothing is allocated or freed. No counterpart in the reference (its
+ * hierarchical launcher always takes caller-owned workspace).
+ */
+#define SILKERN_NOALLOC_MAX_TILES 32768
+int silkern_localize_hierarchical_noalloc_v1(const int32_t* req_ids, const int32_t* block_table,
+                                             int64_t table_rows, int64_t table_width,
+                                             const int32_t* tokens, int32_t* out,
+                                             int32_t* counts, int64_t batch, int64_t width,
+                                             int32_t block_size, int32_t dcp_size,
+                                             int32_t dcp_rank, int32_t dcp_interleave,
+                                             int32_t compact_valid_to_front, int32_t tile_size,
+                                             int32_t* status, void* stream);
 
 /*
  * Device-side equality check used by the CUDA-graph replay gate: adds the

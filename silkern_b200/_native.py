@@ -34,6 +34,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _i32, _i32, _i32, _i32, _i32, _ptr, _ptr],
     ),
     "silkern_workspace_shapes_v1": (_i32, [_i64, _i64, _i32, ctypes.POINTER(_i64)]),
+    "silkern_localize_hierarchical_noalloc_v1": (
+        _i32,
+        [_ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32,
+         _ptr, _ptr],
+    ),
     "silkern_localize_explicit_v1": (
         _i32,
         [_ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i32, _i32, _i32,

@@ -32,6 +32,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 
 #include "fastdiv.cuh"
 #include "ptx.cuh"
@@ -383,6 +384,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
 
   if (crank == 0 && tid == 0) p.counts[row] = row_total;
 }
+
+// Tile workspace of the allocation-free hierarchical entry point: tile counts
+// in the first SILKERN_NOALLOC_MAX_TILES entries, tile offsets in the rest.
+// Loaded with the module on every device that uses the library; shared by all
+// calls. Host code must not pass this symbol to a kernel: its device address
+// comes from cudaGetSymbolAddress (noalloc_scratch below).
+static __device__ __align__(256) int32_t g_noalloc_tiles[2 * SILKERN_NOALLOC_MAX_TILES];
 
 // Adds the number of differing positions to *mismatches.
 __global__ void __launch_bounds__(256) count_mismatches_kernel(const int32_t* a, const int32_t* b,
@@ -766,6 +774,59 @@ extern "C" int silkern_localize_explicit_v1(
   return silkern::launch(r, cluster_size, stage_table, prefetch_table);
 }
 
+namespace silkern {
+namespace {
+
+// Device address of g_noalloc_tiles on the current device, looked up once per
+// device (with that device current) and cached.
+int noalloc_scratch(int32_t** out) {
+  static std::mutex mu;
+  static int32_t* cache[64] = {nullptr};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -static_cast<int>(err);
+  }
+  if (dev < 0 || dev >= 64) return SILKERN_E_SCRATCH;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_noalloc_tiles);
+    if (err != cudaSuccess || ptr == nullptr) {
+      (void)cudaGetLastError();
+      return err != cudaSuccess ? -static_cast<int>(err) : SILKERN_E_SCRATCH;
+    }
+    cache[dev] = static_cast<int32_t*>(ptr);
+  }
+  *out = cache[dev];
+  return SILKERN_OK;
+}
+
+}  // namespace
+}  // namespace silkern
+
+extern "C" int silkern_localize_hierarchical_noalloc_v1(
+    const int32_t* req_ids, const int32_t* block_table, int64_t table_rows, int64_t table_width,
+    const int32_t* tokens, int32_t* out, int32_t* counts, int64_t batch, int64_t width,
+    int32_t block_size, int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave,
+    int32_t compact_valid_to_front, int32_t tile_size, int32_t* status, void* stream) {
+  if (tile_size < SILKERN_MIN_TILE_SIZE || tile_size > SILKERN_MAX_TILE_SIZE ||
+      !silkern::is_pow2(static_cast<uint32_t>(tile_size))) {
+    return SILKERN_E_TILE;
+  }
+  if (batch < 1 || width < 1 || width > SILKERN_MAX_ROW_WIDTH) return SILKERN_E_SHAPE;
+  if (batch * ((width + tile_size - 1) / tile_size) > SILKERN_NOALLOC_MAX_TILES) return SILKERN_E_SCRATCH;
+  int32_t* scratch = nullptr;
+  const int rc = silkern::noalloc_scratch(&scratch);
+  if (rc != SILKERN_OK) return rc;
+  const Request r{req_ids, block_table, table_rows, table_width, tokens, out, counts, scratch,
+                  scratch + SILKERN_NOALLOC_MAX_TILES, batch, width, block_size, dcp_size, dcp_rank,
+                  dcp_interleave, compact_valid_to_front, tile_size, status,
+                  static_cast<cudaStream_t>(stream)};
+  return silkern::launch(r, 0, -1, -1);
+}
+
 extern "C" int silkern_workspace_shapes_v1(int64_t batch, int64_t width, int32_t tile_size,
                                            int64_t out_shapes[8]) {
   if (out_shapes == nullptr) return SILKERN_E_NULL;
@@ -815,6 +876,8 @@ extern "C" const char* silkern_status_string_v1(int code) {
     case SILKERN_E_TILE: return "unsupported tile_size";
     case SILKERN_E_ALIAS: return "an output buffer overlaps an input or another output";
     case SILKERN_E_GEOMETRY: return "explicit launch geometry rejected";
+    case SILKERN_E_SCRATCH:
+      return "batch x tiles exceeds the allocation-free entry point's static workspace";
     default: break;
   }
   if (code < 0) return cudaGetErrorString(static_cast<cudaError_t>(-code));
