@@ -113,7 +113,9 @@ int silkern_workspace_shapes_v1(int64_t batch, int64_t width, int32_t tile_size,
  * stage_table = 1 stages the request's block-table row in shared memory
  * (table_width <= 4096), 0 gathers it from global memory, -1 lets the
  * library decide; prefetch_table likewise for the L2 bulk prefetch of the
- * whole table. tile_size = 0 selects row-wise semantics (no workspace).
+ * whole table; chunks_per_thread (1, 2, 4 or 8; 0 = library choice) sets how
+ * many four-column chunks each thread maps. tile_size = 0 selects row-wise
+ * semantics (no workspace).
  * Same semantics and outputs as the entry points above. No counterpart in the
  * reference (its launch geometry is fixed inside each launcher).
  */
@@ -125,7 +127,8 @@ int silkern_localize_explicit_v1(const int32_t* req_ids, const int32_t* block_ta
                                  int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave,
                                  int32_t compact_valid_to_front, int32_t tile_size,
                                  int32_t cluster_size, int32_t stage_table,
-                                 int32_t prefetch_table, int32_t* status, void* stream);
+                                 int32_t prefetch_table, int32_t chunks_per_thread,
+                                 int32_t* status, void* stream);
 
 /*
  * Hierarchical localization for callers that cannot allocate device memory:

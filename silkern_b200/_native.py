@@ -42,7 +42,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "silkern_localize_explicit_v1": (
         _i32,
         [_ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i32, _i32, _i32,
-         _i32, _i32, _i32, _i32, _i32, _i32, _ptr, _ptr],
+         _i32, _i32, _i32, _i32, _i32, _i32, _i32, _ptr, _ptr],
     ),
     "silkern_count_mismatches_v1": (_i32, [_ptr, _ptr, _i64, _ptr, _ptr]),
     "silkern_status_string_v1": (ctypes.c_char_p, [ctypes.c_int]),

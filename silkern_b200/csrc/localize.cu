@@ -40,7 +40,8 @@
 
 namespace silkern {
 
-constexpr int kMaxThreads = 512;
+constexpr int kMaxThreads = 512;      // threads per row group
+constexpr int kMaxCtaThreads = 1024;  // threads per CTA (row groups of one-chunk rows)
 constexpr int kMaxCluster = 8;
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
 constexpr uint32_t kFull = 0xffffffffu;
@@ -67,8 +68,14 @@ struct Params {
   int32_t compact;        // compaction on (selects the kernel instantiation)
   int32_t tile_shift;     // log2(tile_size) when publishing tiles, else -1
   int32_t tiles_per_row;
-  int32_t smem_row;       // int offset of the survivor stage in dynamic shared memory
-  int32_t smem_tile;      // int offset of the tile offsets in dynamic shared memory
+  int32_t smem_group;     // ints of dynamic shared memory per row group
+  int32_t smem_row;       // offset of the survivor stage in a group's region
+  int32_t smem_wt;        // offset of the warp totals in a group's region
+  int32_t smem_tile;      // offset of the tile offsets in a group's region
+  int32_t row_threads;    // threads per row group (a power of two without a cluster)
+  int32_t row_threads_shift;
+  int32_t rows_base;      // rows per CTA: rows_base, plus one for the first rows_extra CTAs
+  int32_t rows_extra;
   uint32_t dcp_rank;
   uint32_t dcp_size;
   uint32_t interleave;
@@ -113,43 +120,76 @@ __device__ __forceinline__ void copy_from_shared(int32_t* dst, const int32_t* sr
   if (tid < rest) dst[head + 4 * nvec + tid] = src[head + 4 * nvec + tid];
 }
 
+// Copy table row `src` (n entries) into shared memory with cp.async.
+__device__ __forceinline__ void stage_row_async(int32_t* dst, const int32_t* src, int n, int tid,
+                                                int nthreads) {
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+    const int nvec = n >> 2;
+    for (int g = tid; g < nvec; g += nthreads) cp_async_16(dst + 4 * g, src + 4 * g);
+    for (int e = 4 * nvec + tid; e < n; e += nthreads) cp_async_4(dst + e, src + e);
+  } else {
+    for (int e = tid; e < n; e += nthreads) cp_async_4(dst + e, src + e);
+  }
+}
+
 // NC chunks of four columns per thread; CLUSTER: rows split over a cluster;
 // MODE: general arithmetic, all powers of two, or all powers of two with
 // interleave 1; STAGE: the block-table row is staged in shared memory instead
 // of gathered from L2; COMPACT: valid values go to the front of the row.
+//
+// Without a cluster a CTA holds p.rows_base or p.rows_base + 1 consecutive
+// rows, one group of p.row_threads threads per row (each group with its own
+// shared-memory region). Spreading the rows over at most one CTA per SM keeps
+// the load even under programmatic dependent launch: the next call's CTAs
+// become resident where this call left room, and with one-row CTAs several of
+// them could pile onto one SM.
 template <int NC, bool CLUSTER, int MODE, bool STAGE, bool COMPACT>
-__global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_constant__ Params p) {
-  extern __shared__ __align__(16) int32_t smem[];  // [table stage][survivors][tile offsets]
-  __shared__ int32_t s_wt[NC * 32];                // warp totals per chunk
+__global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxThreads,
+                                  (NC == 1 && !CLUSTER) ? 2 : 1)
+    localize_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(16) int32_t smem[];  // per row group: [table][survivors][warp totals][tiles]
   __shared__ int32_t s_cta_total[kMaxCluster];
 
-  const int nthreads = blockDim.x;
-  const int nwarps = nthreads >> 5;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
+  int nthreads, tid, group;
   int64_t row;
   int crank;
+  bool active;
   if constexpr (CLUSTER) {
+    nthreads = blockDim.x;
+    tid = threadIdx.x;
+    group = 0;
     row = cluster_id_x();
     crank = static_cast<int>(cluster_ctarank());
+    active = true;
     cluster_arrive_relaxed();  // phase 0: this CTA is resident
   } else {
-    row = blockIdx.x;
+    nthreads = p.row_threads;
+    group = static_cast<int>(threadIdx.x >> p.row_threads_shift);
+    tid = static_cast<int>(threadIdx.x) & (nthreads - 1);
+    const int extra = static_cast<int>(blockIdx.x) < p.rows_extra ? 1 : 0;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * p.rows_base +
+                          min(static_cast<int>(blockIdx.x), p.rows_extra);
+    active = group < p.rows_base + extra;
+    row = first + (active ? group : 0);
     crank = 0;
   }
+  const int nwarps = nthreads >> 5;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  int32_t* gsmem = smem + group * p.smem_group;
+  int32_t* s_wt = gsmem + p.smem_wt;  // [NC][32] warp totals
   pdl_launch_dependents();
 
   const int c0 = crank * p.slice;
-  const int len = min(p.slice, p.width - c0);
+  const int len = active ? min(p.slice, p.width - c0) : 0;
   const int32_t* tok = p.tokens + row * p.width + c0;
 
-  if (tid == 0) {
+  if (tid == 0 && active) {
     prefetch_l2_line(p.req_ids + row);
     const uintptr_t lo = (reinterpret_cast<uintptr_t>(tok) + 15u) & ~uintptr_t{15};
     const uintptr_t hi = reinterpret_cast<uintptr_t>(tok + len) & ~uintptr_t{15};
     if (hi > lo) prefetch_l2_bulk(reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo));
-    if (p.table_chunk != 0) {
+    if (p.table_chunk != 0 && group == 0) {
       const uint64_t begin = static_cast<uint64_t>(blockIdx.x) * p.table_chunk;
       if (begin < p.table_bytes) {
         const uint64_t end = begin + p.table_chunk < p.table_bytes ? begin + p.table_chunk : p.table_bytes;
@@ -161,6 +201,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
   pdl_wait();  // everything below may read what the previous grid wrote
 
   const int32_t req = __ldg(p.req_ids + row);
+  int32_t* s_tbl = gsmem;
+  if constexpr (STAGE) {
+    // Speculate that row r belongs to request r (one selection row per
+    // request, in order) and start copying that table row into shared memory
+    // now, in parallel with the token loads; repaired below when req != r.
+    if (active && row < p.table_rows) {
+      stage_row_async(s_tbl, p.table + row * p.table_width, static_cast<int>(p.table_width), tid,
+                      nthreads);
+    }
+  }
   const bool tok_vec = (reinterpret_cast<uintptr_t>(tok) & 15u) == 0;
   int32_t val[NC][4];
 #pragma unroll
@@ -183,21 +233,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
     *reinterpret_cast<volatile int32_t*>(p.status) = SILKERN_STATUS_BAD_REQUEST;
   }
   const int32_t* trow = p.table + static_cast<int64_t>(req_ok ? req : 0) * p.table_width;
-
-  int32_t* s_tbl = smem;
   if constexpr (STAGE) {
-    if (req_ok) {
-      const int n = static_cast<int>(p.table_width);
-      if ((reinterpret_cast<uintptr_t>(trow) & 15u) == 0) {
-        const int nvec = n >> 2;
-        const int4* src = reinterpret_cast<const int4*>(trow);
-        int4* dst = reinterpret_cast<int4*>(s_tbl);
-        for (int g = tid; g < nvec; g += nthreads) dst[g] = __ldg(src + g);
-        for (int e = 4 * nvec + tid; e < n; e += nthreads) s_tbl[e] = __ldg(trow + e);
-      } else {
-        for (int e = tid; e < n; e += nthreads) s_tbl[e] = __ldg(trow + e);
-      }
+    if (req_ok && static_cast<int64_t>(req) != row) {  // the same for every thread of the CTA
+      // Every thread's speculative copies must land before any repair copy
+      // is issued: the two rows can differ in 16-byte alignment, and then the
+      // two passes split the entries between threads differently.
+      cp_async_wait_all();
+      __syncthreads();
+      stage_row_async(s_tbl, trow, static_cast<int>(p.table_width), tid, nthreads);
     }
+    cp_async_wait_all();
     __syncthreads();
   }
 
@@ -294,7 +339,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
   if constexpr (COMPACT) {
     // Stage this CTA's survivors compactly in shared memory, then write them
     // and the -1 tail with 128-bit stores, each output element once.
-    int32_t* s_row = smem + p.smem_row;
+    int32_t* s_row = gsmem + p.smem_row;
 #pragma unroll
     for (int i = 0; i < NC; ++i) {
       int32_t* dst = s_row + base[i] + lane_pre[i];
@@ -357,7 +402,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
   if (p.tile_shift >= 0) {
     // Publish the tile decomposition: the exclusive position of the element
     // in a tile's first column is that tile's offset; counts are differences.
-    int32_t* s_tile = smem + p.smem_tile;
+    int32_t* s_tile = gsmem + p.smem_tile;
     const int tmask = (1 << p.tile_shift) - 1;
 #pragma unroll
     for (int i = 0; i < NC; ++i) {
@@ -382,7 +427,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) localize_kernel(const __grid_c
     }
   }
 
-  if (crank == 0 && tid == 0) p.counts[row] = row_total;
+  if (crank == 0 && tid == 0 && active) p.counts[row] = row_total;
 }
 
 // Tile workspace of the allocation-free hierarchical entry point: tile counts
@@ -540,20 +585,54 @@ int validate(const Request& r) {
 struct Geometry {
   int cluster;
   int slice;
-  int threads;
+  int threads;  // per row group
   int nc;
   bool stage;
   bool prefetch;
+  int rows_per_cta;   // row groups per CTA (1 with a cluster)
+  int64_t row_ctas;   // CTAs over the batch (times `cluster` for the grid)
 };
+
+uint32_t next_pow2(uint32_t v) {
+  uint32_t p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+// Shared memory per SM and reserved per CTA, for occupancy shaping.
+void smem_limits(int* per_sm, int* reserved) {
+  static int cache_sm[64] = {0}, cache_res[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    (void)cudaGetLastError();
+    *per_sm = 233472;
+    *reserved = 1024;
+    return;
+  }
+  if (cache_sm[dev] == 0) {
+    int a = 0, b = 0;
+    if (cudaDeviceGetAttribute(&a, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess || a <= 0) a = 233472;
+    if (cudaDeviceGetAttribute(&b, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess || b < 0) b = 1024;
+    (void)cudaGetLastError();
+    cache_res[dev] = b;
+    cache_sm[dev] = a;
+  }
+  *per_sm = cache_sm[dev];
+  *reserved = cache_res[dev];
+}
 
 // Chunks of four columns per thread and threads per CTA for `slice` columns:
 // up to kMaxThreads threads with one chunk each, then more chunks per thread
 // (short per-thread dependency chains measured faster than fewer, longer ones).
-bool fit_slice(int slice, int* nc, int* threads) {
+bool fit_slice(int slice, int nc_req, int* nc, int* threads) {
   const int granules = (slice + 3) / 4;
   int c = 1;
-  while (granules > c * kMaxThreads) c *= 2;
-  if (c > 8) return false;
+  if (nc_req > 0) {
+    c = nc_req;
+  } else {
+    while (granules > c * kMaxThreads) c *= 2;
+  }
+  if (c > 8 || granules > c * kMaxThreads) return false;
   int t = (granules + c - 1) / c;
   t = (t + 31) / 32 * 32;
   *nc = c;
@@ -561,7 +640,8 @@ bool fit_slice(int slice, int* nc, int* threads) {
   return true;
 }
 
-int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefetch_req, Geometry* g) {
+int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefetch_req, int nc_req,
+                    Geometry* g) {
   const int width = static_cast<int>(r.width);
   int cs;
   int slice;
@@ -596,9 +676,28 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
   }
   if (cluster_req > 0 && cs != cluster_req) return SILKERN_E_GEOMETRY;
   if (cs < 1 || cs > kMaxCluster) return SILKERN_E_GEOMETRY;
-  if (!fit_slice(slice, &g->nc, &g->threads)) return SILKERN_E_GEOMETRY;
+  if (!fit_slice(slice, nc_req, &g->nc, &g->threads)) return SILKERN_E_GEOMETRY;
   g->cluster = cs;
   g->slice = slice;
+  g->rows_per_cta = 1;
+  g->row_ctas = r.batch;
+  if (cs == 1) {
+    // Row groups: a power-of-two group per row; one-chunk rows are packed
+    // into CTAs of up to 1024 threads, with the rows spread over at most one
+    // CTA per SM.
+    g->threads = static_cast<int>(next_pow2(static_cast<uint32_t>(g->threads)));
+    if (g->nc == 1) {
+      const int64_t max_rows = kMaxCtaThreads / g->threads;
+      int64_t ctas = r.batch < sm_count() ? r.batch : sm_count();
+      int64_t rows = (r.batch + ctas - 1) / ctas;
+      if (rows > max_rows) {
+        rows = max_rows;
+        ctas = (r.batch + rows - 1) / rows;
+      }
+      g->rows_per_cta = static_cast<int>(rows);
+      g->row_ctas = ctas;
+    }
+  }
   if (stage_req == 1 && r.table_width > kTableStageMax) return SILKERN_E_GEOMETRY;
   g->stage = stage_req == 1;
   const int64_t table_bytes = r.table_rows * r.table_width * 4;
@@ -606,7 +705,7 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
   const bool possible = aligned && table_bytes >= 16 && table_bytes <= (int64_t{1} << 32);
   g->prefetch = prefetch_req >= 0 ? (prefetch_req == 1 && possible)
                                    : (possible && table_bytes <= 2 * r.batch * r.width * 4);
-  if (r.batch * cs > INT32_MAX) return SILKERN_E_SHAPE;
+  if (g->row_ctas * cs > INT32_MAX) return SILKERN_E_SHAPE;
   return SILKERN_OK;
 }
 
@@ -621,11 +720,11 @@ int allow_large_smem(KernelFn fn, size_t bytes) {
   return SILKERN_OK;
 }
 
-int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req) {
+int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req, int nc_req) {
   int rc = validate(r);
   if (rc != SILKERN_OK) return rc;
   Geometry g;
-  rc = choose_geometry(r, cluster_req, stage_req, prefetch_req, &g);
+  rc = choose_geometry(r, cluster_req, stage_req, prefetch_req, nc_req, &g);
   if (rc != SILKERN_OK) return rc;
 
   Params p{};
@@ -645,7 +744,11 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req) {
   p.compact = (r.compact_flag != 0 && r.dcp_size > 1) ? 1 : 0;
   p.tile_shift = r.tile_size ? static_cast<int32_t>(log2_exact(static_cast<uint32_t>(r.tile_size))) : -1;
   p.tiles_per_row = r.tile_size ? static_cast<int32_t>((r.width + r.tile_size - 1) / r.tile_size) : 0;
-  const int64_t grid = r.batch * g.cluster;
+  const int64_t grid = g.row_ctas * g.cluster;
+  p.row_threads = g.threads;
+  p.row_threads_shift = static_cast<int32_t>(log2_exact(static_cast<uint32_t>(g.threads)));
+  p.rows_base = static_cast<int32_t>(r.batch / g.row_ctas);
+  p.rows_extra = static_cast<int32_t>(r.batch % g.row_ctas);
   if (g.prefetch) {
     const uint64_t bytes = static_cast<uint64_t>(r.table_rows * r.table_width * 4) & ~uint64_t{15};
     uint64_t chunk = (bytes + static_cast<uint64_t>(grid) - 1) / static_cast<uint64_t>(grid);
@@ -684,12 +787,24 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req) {
   KernelFn fn = pick_kernel(g.nc, g.cluster > 1, mode, g.stage, p.compact != 0);
   if (fn == nullptr) return SILKERN_E_GEOMETRY;
   const int ntiles_cta = r.tile_size ? (g.slice + r.tile_size - 1) / r.tile_size : 0;
-  // dynamic shared memory: [table stage][survivor stage (16-byte aligned)][tile offsets]
+  // dynamic shared memory per row group: [table stage][survivor stage][warp
+  // totals][tile offsets], every part 16-byte aligned
   const int stage_ints = g.stage ? static_cast<int>((r.table_width + 3) / 4 * 4) : 0;
   const int row_ints = p.compact ? (g.slice + 3) / 4 * 4 : 0;
   p.smem_row = stage_ints;
-  p.smem_tile = stage_ints + row_ints;
-  const size_t smem = sizeof(int32_t) * static_cast<size_t>(stage_ints + row_ints + ntiles_cta);
+  p.smem_wt = stage_ints + row_ints;
+  p.smem_tile = p.smem_wt + g.nc * 32;
+  p.smem_group = (p.smem_tile + ntiles_cta + 3) / 4 * 4;
+  size_t smem = sizeof(int32_t) * static_cast<size_t>(p.smem_group) * static_cast<size_t>(g.rows_per_cta);
+  if (g.cluster == 1 && grid <= sm_count()) {
+    // At most two CTAs of this kernel per SM: the running call and the next
+    // one waiting on it, so the next call's CTAs spread over the SMs instead
+    // of piling onto the ones this call left room on.
+    int per_sm = 0, reserved = 0;
+    smem_limits(&per_sm, &reserved);
+    const size_t two_per_sm = static_cast<size_t>(per_sm / 3 - reserved + 16);
+    if (smem < two_per_sm) smem = two_per_sm;
+  }
   if (smem > 48 * 1024) {
     rc = allow_large_smem(fn, smem);
     if (rc != SILKERN_OK) return rc;
@@ -697,7 +812,7 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req) {
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-  cfg.blockDim = dim3(static_cast<unsigned>(g.threads), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(g.threads * g.rows_per_cta), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = r.stream;
   cudaLaunchAttribute attrs[2];
@@ -737,7 +852,7 @@ extern "C" int silkern_localize_rowwise_v1(const int32_t* req_ids, const int32_t
   const Request r{req_ids, block_table, table_rows, table_width, tokens, out, counts, nullptr, nullptr,
                   batch, width, block_size, dcp_size, dcp_rank, dcp_interleave,
                   compact_valid_to_front, 0, status, static_cast<cudaStream_t>(stream)};
-  return silkern::launch(r, 0, -1, -1);
+  return silkern::launch(r, 0, -1, -1, 0);
 }
 
 extern "C" int silkern_localize_hierarchical_v1(
@@ -753,7 +868,7 @@ extern "C" int silkern_localize_hierarchical_v1(
                   tile_counts_ws, tile_offsets_ws, batch, width, block_size, dcp_size, dcp_rank,
                   dcp_interleave, compact_valid_to_front, tile_size, status,
                   static_cast<cudaStream_t>(stream)};
-  return silkern::launch(r, 0, -1, -1);
+  return silkern::launch(r, 0, -1, -1, 0);
 }
 
 extern "C" int silkern_localize_explicit_v1(
@@ -761,17 +876,21 @@ extern "C" int silkern_localize_explicit_v1(
     const int32_t* tokens, int32_t* out, int32_t* counts, int32_t* tile_counts_ws,
     int32_t* tile_offsets_ws, int64_t batch, int64_t width, int32_t block_size, int32_t dcp_size,
     int32_t dcp_rank, int32_t dcp_interleave, int32_t compact_valid_to_front, int32_t tile_size,
-    int32_t cluster_size, int32_t stage_table, int32_t prefetch_table, int32_t* status,
-    void* stream) {
+    int32_t cluster_size, int32_t stage_table, int32_t prefetch_table, int32_t chunks_per_thread,
+    int32_t* status, void* stream) {
   if (cluster_size < 1 || cluster_size > silkern::kMaxCluster) return SILKERN_E_GEOMETRY;
   if (stage_table < -1 || stage_table > 1 || prefetch_table < -1 || prefetch_table > 1) {
+    return SILKERN_E_GEOMETRY;
+  }
+  if (chunks_per_thread != 0 && chunks_per_thread != 1 && chunks_per_thread != 2 &&
+      chunks_per_thread != 4 && chunks_per_thread != 8) {
     return SILKERN_E_GEOMETRY;
   }
   const Request r{req_ids, block_table, table_rows, table_width, tokens, out, counts,
                   tile_counts_ws, tile_offsets_ws, batch, width, block_size, dcp_size, dcp_rank,
                   dcp_interleave, compact_valid_to_front, tile_size, status,
                   static_cast<cudaStream_t>(stream)};
-  return silkern::launch(r, cluster_size, stage_table, prefetch_table);
+  return silkern::launch(r, cluster_size, stage_table, prefetch_table, chunks_per_thread);
 }
 
 namespace silkern {
@@ -824,7 +943,7 @@ extern "C" int silkern_localize_hierarchical_noalloc_v1(
                   scratch + SILKERN_NOALLOC_MAX_TILES, batch, width, block_size, dcp_size, dcp_rank,
                   dcp_interleave, compact_valid_to_front, tile_size, status,
                   static_cast<cudaStream_t>(stream)};
-  return silkern::launch(r, 0, -1, -1);
+  return silkern::launch(r, 0, -1, -1, 0);
 }
 
 extern "C" int silkern_workspace_shapes_v1(int64_t batch, int64_t width, int32_t tile_size,

@@ -280,6 +280,7 @@ def localize_explicit(
     cluster_size: int = 1,
     stage_table: int = -1,
     prefetch_table: int = -1,
+    chunks_per_thread: int = 0,
     tile_size: int = 0,
     tile_counts=None,
     tile_offsets=None,
@@ -288,7 +289,8 @@ def localize_explicit(
     """Localization with an explicit launch geometry (conformance sweeps, tuning).
 
     Same outputs as the two public launchers; ``cluster_size`` CTAs per row,
-    ``stage_table``/``prefetch_table`` 1, 0 or -1 (library choice). With
+    ``stage_table``/``prefetch_table`` 1, 0 or -1 (library choice),
+    ``chunks_per_thread`` 1, 2, 4, 8 or 0 (library choice). With
     ``tile_size`` > 0 the hierarchical tile workspace is published. Buffers
     are checked by the C ABI only.
     """
@@ -319,6 +321,7 @@ def localize_explicit(
             int(cluster_size),
             int(stage_table),
             int(prefetch_table),
+            int(chunks_per_thread),
             ptr(status),
             stream,
         )

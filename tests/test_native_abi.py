@@ -142,10 +142,10 @@ def test_hierarchical_rejects_before_launch(lib) -> None:
 
 
 def test_explicit_rejects_bad_geometry(lib) -> None:
-    def call(cluster, stage=-1, prefetch=-1, width=16):
+    def call(cluster, stage=-1, prefetch=-1, width=16, chunks=0):
         return lib.silkern_localize_explicit_v1(
             REQ, TABLE, 4, 8, TOK, OUT, CNT, None, None, 4, width, 64, 2, 0, 1, 1, 0, cluster,
-            stage, prefetch, None, None,
+            stage, prefetch, chunks, None, None,
         )
 
     assert call(0) == 7
@@ -153,3 +153,5 @@ def test_explicit_rejects_bad_geometry(lib) -> None:
     assert call(1, stage=2) == 7
     assert call(1, prefetch=-2) == 7
     assert call(8, width=16) == 7  # 8 CTAs cannot each own 4-column slices of 16 columns
+    assert call(1, chunks=3) == 7
+    assert call(1, chunks=1, width=16384) == 7  # 4096 granules do not fit 512 threads x 1 chunk
