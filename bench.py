@@ -1,23 +1,29 @@
-"""Benchmark of the localization converter on B200: the headline selection batch.
+"""Benchmark of the localization converter on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
 
-Workload (one step = one converter call): a selection batch of 256 requests x
-top_k 2048 int32 positions, per-request context U[1024, 65536] (shorter rows
-padded with -1), block_size 64, dcp_size 4, block table (256, 256) over a
-65536-block pool; seeded synthetic data. Each GPU runs the DCP rank
-``gpu_index % 4`` on its own inputs, with no collective on the data path, so
-the per-GPU work is fixed as N grows (weak scaling); rank processes meet only
-on a host barrier and a max-reduction of the timed duration.
+Default workload (config 3, one step = one converter call): a selection batch
+of 256 requests x top_k 2048 int32 positions, per-request context
+U[1024, 65536] (shorter rows padded with -1), block_size 64, dcp_size 4, block
+table (256, 256) over a 65536-block pool; seeded synthetic data. Other
+configs: 2 (64 x 2048, dcp 2), 4 (32 x 16384 through the hierarchical entry
+point, tile 1024, dcp 8) and 5 (one step = a 48-layer decode step, 48 calls of
+128 x 2048, dcp 8).
 
-Timed region (our arm): K row-wise calls captured in CUDA graphs and replayed
-on one stream, bracketed by CUDA events; inputs rotate over 64 resident
-buffer sets (about 275 MB, more than twice the 126 MB L2), so every call
-reads cold data. ``value`` is localized indices per second over all GPUs;
-``e2e`` is the same metric through the public Python API with the inputs
-copied from pinned host memory and the results copied back every step.
-After timing, every buffer set's output is compared with the oracle.
+Each GPU runs the DCP rank ``gpu_index % dcp_size`` on its own inputs, with no
+collective on the data path, so the per-GPU work is fixed as N grows (weak
+scaling); rank processes meet only on a host barrier and a max-reduction of
+the timed duration.
+
+Timed region (our arm): W warm-up steps, then exactly K steps, all captured in
+CUDA graphs and replayed on one stream, bracketed by CUDA events. Inputs
+rotate over enough resident buffer sets to exceed twice the 126 MB L2, so
+every call reads data that is not already in L2. ``value`` is localized
+indices per second over all GPUs; ``e2e`` is the same metric through the
+public Python API with the inputs copied from pinned host memory and the
+results copied back every step. After timing, every buffer set's output is
+compared with the oracle (``bit_exact``).
 
 ``--impl reference`` times the reference algorithm on the host instead: the C
 restatement of the reference's ``localize_reference`` (oracle/) with every
@@ -28,7 +34,9 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
+import re
 import statistics
 import sys
 import threading
@@ -38,38 +46,92 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 if REPO not in sys.path:
     sys.path.insert(0, REPO)
 
-CONFIG = 3
-DCP_SIZE = 4
-BUFFER_SETS = 64
+L2_BYTES = 126 * 1024 * 1024
 DISTINCT_CASES = 8
-CHUNK = 256  # calls per captured graph
-METRIC = "Gindices/s per B200 at 256x2048 (localized selection indices per second)"
+CHUNK = 256  # launches per captured graph
 UNIT = "Gindices/s"
+METRIC = "Gindices/s per B200 at 256x2048 (localized selection indices per second)"
+
+WORKLOADS = {
+    2: {"desc": "config2: batch 64 x top_k 2048 int32, seq 32768, block_size 64, dcp_size 2, "
+                "table (64,256)", "dcp_size": 2, "calls": 1, "arm": "row_stable"},
+    3: {"desc": "config3: batch 256 x top_k 2048 int32, seq U[1024,65536] with -1 padding, "
+                "block_size 64, dcp_size 4, table (256,256)", "dcp_size": 4, "calls": 1,
+        "arm": "row_stable"},
+    4: {"desc": "config4: batch 32 x top_k 16384 int32, seq 131072, hierarchical tile 1024, "
+                "block_size 64, dcp_size 8, table (32,256)", "dcp_size": 8, "calls": 1,
+        "arm": "hierarchical_stable"},
+    5: {"desc": "config5: 48-layer decode step, each layer batch 128 x top_k 2048 int32, "
+                "seq 32768, block_size 64, dcp_size 8, table (128,64)", "dcp_size": 8, "calls": 48,
+        "arm": "row_stable"},
+}
 
 
 def _peaks() -> dict:
-    path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
-        with open(path) as fh:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
             data = json.load(fh)
         return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured (MEASURED_PEAKS.json)"}
     except (OSError, KeyError, ValueError):
         return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def _workload_config(rank: int, world: int) -> dict:
+def _traffic(config: int) -> dict | None:
+    """DRAM bytes per launch from the committed ncu summary of this workload, if any."""
+    name = WORKLOADS[config]["arm"].replace("_stable", "")
+    path = os.path.join(REPO, "profiles", f"localize_{name}_config{config}.md")
+    try:
+        with open(path) as fh:
+            text = fh.read()
+    except OSError:
+        return None
+    match = re.search(r"dram_bytes_per_launch:\s*(\d+)", text)
+    return {"bytes": int(match.group(1)), "source": os.path.relpath(path, REPO)} if match else None
+
+
+def _case(config: int, *, seed: int, dcp_rank: int):
+    from silkern_b200.workloads import config_case
+
+    return config_case(config, seed=seed, dcp_rank=dcp_rank)
+
+
+def _workload_config(config: int, world: int, n_sets: int) -> dict:
+    w = WORKLOADS[config]
+    case = _case(config, seed=0, dcp_rank=0)
     return {
-        "workload": "config3: batch 256 x top_k 2048 int32, seq U[1024,65536] with -1 padding, "
-                    "block_size 64, dcp_size 4, table (256,256)",
-        "batch": 256,
-        "top_k": 2048,
-        "dcp_size": DCP_SIZE,
-        "dcp_rank": "gpu_index % 4",
-        "block_size": 64,
-        "arm": "row_stable (localize_rowwise)",
-        "l2": f"inputs larger than L2: {BUFFER_SETS} rotating buffer sets",
+        "workload": w["desc"],
+        "batch": case.batch,
+        "top_k": case.width,
+        "dcp_size": w["dcp_size"],
+        "dcp_rank": f"gpu_index % {w['dcp_size']}",
+        "block_size": case.block_size,
+        "calls_per_step": w["calls"],
+        "arm": w["arm"],
+        "l2": f"inputs larger than L2: {n_sets} rotating buffer sets",
         "parallelism": f"{world} independent DCP-rank shards, no data-path collective",
     }
+
+
+def shard_plan(rank: int, world: int, config: int = 3) -> dict:
+    """What one rank converts: its DCP rank and the seed of its own inputs.
+
+    Ranks are independent shards (no data is exchanged); rank r converts the
+    DCP rank r % dcp_size on inputs seeded by its global rank.
+    """
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    return {"dcp_rank": rank % WORKLOADS[config]["dcp_size"], "base_seed": 1000 * (rank + 1)}
+
+
+def reduce_max(dist, value: float) -> float:
+    """Max of a host float over all ranks (gloo), or the value itself without dist."""
+    if dist is None:
+        return float(value)
+    import torch
+
+    t = torch.tensor([float(value)], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 class ClockSampler:
@@ -144,55 +206,6 @@ class ClockSampler:
         }
 
 
-def _cpu_baseline(threads: int, seconds: float = 2.0) -> dict:
-    """The C oracle (restatement of the reference's localize_reference) on host cores."""
-    import oracle
-    from silkern_b200.workloads import config_case
-
-    case = config_case(CONFIG, seed=0, dcp_rank=0)
-    kw = case.geometry()
-    oracle.localize(case.req_ids, case.block_table, case.tokens, threads=threads, **kw)
-    calls = 0
-    start = time.perf_counter()
-    while True:
-        oracle.localize(case.req_ids, case.block_table, case.tokens, threads=threads, **kw)
-        calls += 1
-        elapsed = time.perf_counter() - start
-        if elapsed >= seconds and calls >= 3:
-            break
-    rate = calls * case.batch * case.width / elapsed / 1e9
-    return {
-        "value": rate,
-        "unit": UNIT,
-        "cores": threads,
-        "kind": "port",
-        "sample": f"{calls} full calls of the 256x2048 dcp-4 rank-0 batch in {elapsed:.2f} s "
-                  f"({threads} threads, oracle/localize_oracle.c)",
-    }
-
-
-def shard_plan(rank: int, world: int) -> dict:
-    """What one rank converts: its DCP rank and the seed of its own inputs.
-
-    Ranks are independent shards (no data is exchanged); rank r converts the
-    DCP rank r % 4 on inputs seeded by its global rank.
-    """
-    if not 0 <= rank < world:
-        raise ValueError(f"rank {rank} outside world of {world}")
-    return {"dcp_rank": rank % DCP_SIZE, "base_seed": 1000 * (rank + 1)}
-
-
-def reduce_max(dist, value: float) -> float:
-    """Max of a host float over all ranks (gloo), or the value itself without dist."""
-    if dist is None:
-        return float(value)
-    import torch
-
-    t = torch.tensor([float(value)], dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
 def _host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -200,49 +213,91 @@ def _host_threads() -> int:
         return os.cpu_count() or 1
 
 
+def _oracle_step(cases, threads: int) -> None:
+    import oracle
+
+    for case in cases:
+        oracle.localize(case.req_ids, case.block_table, case.tokens, threads=threads, **case.geometry())
+
+
+def _cpu_baseline(config: int, threads: int, seconds: float = 2.0) -> dict:
+    """The C oracle (restatement of the reference's localize_reference) on host cores."""
+    calls = WORKLOADS[config]["calls"]
+    cases = [_case(config, seed=layer, dcp_rank=0) for layer in range(calls)]
+    _oracle_step(cases[:1], threads)
+    steps = 0
+    start = time.perf_counter()
+    while True:
+        _oracle_step(cases, threads)
+        steps += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds and steps >= 3:
+            break
+    indices = calls * cases[0].batch * cases[0].width
+    return {
+        "value": steps * indices / elapsed / 1e9,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{steps} full steps ({calls} call(s) of {cases[0].batch}x{cases[0].width}) in "
+                  f"{elapsed:.2f} s, {threads} threads, oracle/localize_oracle.c",
+    }
+
+
 def run_reference(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
-    import oracle
-    from silkern_b200.workloads import config_case
-
+    config = args.config
     threads = _host_threads()
-    case = config_case(CONFIG, seed=0, dcp_rank=0)
-    kw = case.geometry()
+    calls = WORKLOADS[config]["calls"]
+    cases = [_case(config, seed=layer, dcp_rank=0) for layer in range(calls)]
     for _ in range(args.warmup):
-        oracle.localize(case.req_ids, case.block_table, case.tokens, threads=threads, **kw)
+        _oracle_step(cases, threads)
     start = time.perf_counter()
     for _ in range(args.steps):
-        oracle.localize(case.req_ids, case.block_table, case.tokens, threads=threads, **kw)
+        _oracle_step(cases, threads)
     elapsed = time.perf_counter() - start
     per_step = elapsed / args.steps
-    value = case.batch * case.width / per_step / 1e9
+    indices = calls * cases[0].batch * cases[0].width
+    value = indices / per_step / 1e9
     return {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": METRIC if config == 3 else f"Gindices/s per B200, config {config}",
         "value": value,
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": per_step * 1e3,
-        "us_per_call": per_step * 1e6,
+        "us_per_call": per_step * 1e6 / calls,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "int32",
         "data": "synthetic (seeded)",
-        "config": _workload_config(0, 1),
+        "config": _workload_config(config, 1, 0),
         "cpu_baseline": {
             "value": value,
             "unit": UNIT,
             "cores": threads,
             "kind": "port",
-            "sample": f"{args.steps} full calls of the 256x2048 dcp-4 rank-0 batch, {threads} threads "
-                      "(C restatement of silkern/contract.py:67-158 in oracle/localize_oracle.c)",
+            "sample": f"{args.steps} full steps, {threads} threads (C restatement of "
+                      "silkern/contract.py:67-158 in oracle/localize_oracle.c)",
         },
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def _make_call(arm: str, bufs: dict, geometry: dict, tile_size: int):
+    from silkern_b200.kernels import localize_hierarchical, localize_rowwise
+
+    if arm == "row_stable":
+        return lambda: localize_rowwise(bufs["req"], bufs["table"], bufs["tokens"], bufs["out"],
+                                        bufs["counts"], **geometry)
+    return lambda: localize_hierarchical(
+        bufs["req"], bufs["table"], bufs["tokens"], bufs["out"], bufs["counts"], bufs["mapped"],
+        bufs["local_positions"], bufs["tile_counts"], bufs["tile_offsets"], tile_size=tile_size,
+        **geometry)
 
 
 def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
@@ -250,61 +305,62 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     import torch
 
     import oracle
-    import silkern_b200 as silkern
-    from silkern_b200.kernels import localize_rowwise
-    from silkern_b200.workloads import config_case
+    from silkern_b200 import _native
+    from silkern_b200.workspace import workspace_shapes
 
+    config = args.config
+    spec = WORKLOADS[config]
+    calls = spec["calls"]
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    plan = shard_plan(rank, world)
-    dcp_rank = plan["dcp_rank"]
-    base_seed = plan["base_seed"]
+    plan = shard_plan(rank, world, config)
 
-    # Distinct seeded cases, laid out in BUFFER_SETS separate resident buffer sets.
-    cases = [config_case(CONFIG, seed=base_seed + i, dcp_rank=dcp_rank) for i in range(DISTINCT_CASES)]
+    distinct = calls if calls > 1 else DISTINCT_CASES
+    cases = [_case(config, seed=plan["base_seed"] + i, dcp_rank=plan["dcp_rank"]) for i in range(distinct)]
+    bytes_per_call = cases[0].algorithmic_bytes()
+    n_sets = max(64, math.ceil(2.05 * L2_BYTES / bytes_per_call))
+    n_sets = math.ceil(n_sets / distinct) * distinct
     sets = []
-    for i in range(BUFFER_SETS):
-        case = cases[i % DISTINCT_CASES]
-        req, table, tokens = (torch.as_tensor(a).to(dev) for a in (case.req_ids, case.block_table, case.tokens))
-        out = torch.empty_like(tokens)
-        counts = torch.empty(case.batch, dtype=torch.int32, device=dev)
-        sets.append((req, table, tokens, out, counts))
-    geometry = cases[0].geometry()
-    algorithmic = cases[0].algorithmic_bytes()
+    for i in range(n_sets):
+        case = cases[i % distinct]
+        bufs = {name: torch.as_tensor(a).to(dev) for name, a in
+                (("req", case.req_ids), ("table", case.block_table), ("tokens", case.tokens))}
+        bufs["out"] = torch.empty_like(bufs["tokens"])
+        bufs["counts"] = torch.empty(case.batch, dtype=torch.int32, device=dev)
+        if spec["arm"] == "hierarchical_stable":
+            for name, shape in workspace_shapes(case.batch, case.width, tile_size=case.tile_size).items():
+                bufs[name] = torch.empty(shape, dtype=torch.int32, device=dev)
+        sets.append((bufs, _make_call(spec["arm"], bufs, case.geometry(), case.tile_size)))
     indices_per_call = cases[0].batch * cases[0].width
 
-    def call(i: int) -> None:
-        req, table, tokens, out, counts = sets[i % BUFFER_SETS]
-        localize_rowwise(req, table, tokens, out, counts, **geometry)
+    def launch(i: int) -> None:
+        sets[i % n_sets][1]()
 
-    # Eager warm-up (also loads the library and its kernels) on a side stream.
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(stream):
-        for i in range(max(3, BUFFER_SETS)):
-            call(i)
+        for i in range(max(3, n_sets)):
+            launch(i)
     torch.cuda.synchronize(dev)
 
-    def capture(first: int, count: int):
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(first, first + count):
-                call(i)
-        return graph
-
-    def plan(steps: int):
+    def plan_graphs(first: int, count: int):
         graphs = []
         done = 0
-        while done < steps:
-            count = min(CHUNK, steps - done)
-            graphs.append(capture(done, count))
-            done += count
+        while done < count:
+            n = min(CHUNK, count - done)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(first + done, first + done + n):
+                    launch(i)
+            graphs.append(graph)
+            done += n
         return graphs
 
-    warm_graphs = plan(args.warmup)
-    main_graphs = plan(args.steps)
+    warm_launches = args.warmup * calls
+    timed_launches = args.steps * calls
+    warm_graphs = plan_graphs(0, warm_launches)
+    main_graphs = plan_graphs(warm_launches, timed_launches)
     torch.cuda.synchronize(dev)
-
     with torch.cuda.stream(stream):
         for g in warm_graphs:
             g.replay()
@@ -327,44 +383,42 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     if dist is not None:
         dist.barrier()
     elapsed_ms = reduce_max(dist, start.elapsed_time(end))
-    per_call_s = elapsed_ms / 1e3 / args.steps
+    per_step_s = elapsed_ms / 1e3 / args.steps
+    per_call_s = per_step_s / calls
 
-    # The timed outputs must be the reference's: check every buffer set.
+    # The timed outputs must be the reference's: check every buffer set used.
     expected = [oracle.localize(c.req_ids, c.block_table, c.tokens, threads=4, **c.geometry())
                 for c in cases]
+    used = {i % n_sets for i in range(warm_launches + timed_launches)}
     bit_exact = True
-    last_use = {}
-    for i in range(args.steps):
-        last_use[i % BUFFER_SETS] = True
-    for index, (_, _, _, out, counts) in enumerate(sets):
-        if index not in last_use:
-            continue
-        want_out, want_counts = expected[index % DISTINCT_CASES]
-        if not (np.array_equal(out.cpu().numpy(), want_out)
-                and np.array_equal(counts.cpu().numpy(), want_counts)):
+    for index in sorted(used):
+        bufs = sets[index][0]
+        want_out, want_counts = expected[index % distinct]
+        if not (np.array_equal(bufs["out"].cpu().numpy(), want_out)
+                and np.array_equal(bufs["counts"].cpu().numpy(), want_counts)):
             bit_exact = False
     del warm_graphs, main_graphs
 
-    e2e = run_e2e(args, cases[0], dev, geometry, dist)
+    e2e = run_e2e(args, cases[:calls], dev, dist)
 
-    value = world * indices_per_call / per_call_s / 1e9
     peaks = _peaks()
-    achieved = algorithmic / per_call_s / 1e9
+    achieved = bytes_per_call / per_call_s / 1e9
+    traffic = _traffic(config)
     result = {
-        "metric": METRIC,
-        "value": value,
+        "metric": METRIC if config == 3 else f"Gindices/s per B200, config {config}",
+        "value": world * calls * indices_per_call / per_step_s / 1e9,
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": per_call_s * 1e3,
+        "ms_per_step": per_step_s * 1e3,
         "us_per_call": per_call_s * 1e6,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "int32",
-        "data": "synthetic (seeded; config 3 shapes)",
-        "config": _workload_config(rank, world),
+        "data": f"synthetic (seeded; config {config} shapes)",
+        "config": _workload_config(config, world, n_sets),
         "bit_exact": bit_exact,
         "hbm_gbs": achieved,
         "roofline": {
@@ -373,59 +427,87 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
             "peak": peaks["hbm_gbs"],
             "unit": "GB/s",
             "frac": achieved / peaks["hbm_gbs"],
-            "traffic": None,
-            "algorithmic_bytes_per_call": algorithmic,
+            "traffic": traffic["bytes"] if traffic else None,
+            "traffic_source": traffic["source"] if traffic else None,
+            "algorithmic_bytes_per_call": bytes_per_call,
             "peak_source": peaks["source"],
             "timing": "CUDA events around the graph replays of the timed calls, per call",
         },
-        "gpu_launches": args.steps,
+        "gpu_launches": timed_launches,
         "e2e": e2e,
         "clocks": sampler.summary(),
-        "library": silkern._native.LIB_PATH if hasattr(silkern, "_native") else None,
+        "library": _native.LIB_PATH,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = _cpu_baseline(_host_threads())
+        result["cpu_baseline"] = _cpu_baseline(config, _host_threads())
     return result if rank == 0 else None
 
 
-def run_e2e(args, case, dev, geometry, dist) -> dict:
+def run_e2e(args, cases, dev, dist) -> dict:
     """Same metric through the public API, host inputs in and results out every step."""
     import torch
 
-    from silkern_b200.kernels import localize_rowwise
+    from silkern_b200.workspace import workspace_shapes
 
     steps = args.e2e_steps if args.e2e_steps > 0 else args.steps
-    batch, width = case.tokens.shape
-    n_req, n_table = case.req_ids.size, case.block_table.size
-    n_in = n_req + n_table + case.tokens.size
-    host_in = torch.empty(n_in, dtype=torch.int32).pin_memory()
-    host_in[:n_req] = torch.as_tensor(case.req_ids)
-    host_in[n_req:n_req + n_table] = torch.as_tensor(case.block_table.ravel())
-    host_in[n_req + n_table:] = torch.as_tensor(case.tokens.ravel())
+    arm = WORKLOADS[args.config]["arm"]
     lanes = []
-    for _ in range(2):
-        # Inputs share one device buffer (one H2D copy); the two outputs must
-        # not share storage, so they come back in two D2H copies.
-        dev_in = torch.empty(n_in, dtype=torch.int32, device=dev)
-        out = torch.empty((batch, width), dtype=torch.int32, device=dev)
-        counts = torch.empty(batch, dtype=torch.int32, device=dev)
-        host_out = torch.empty((batch, width), dtype=torch.int32).pin_memory()
-        host_counts = torch.empty(batch, dtype=torch.int32).pin_memory()
-        req = dev_in[:n_req]
-        table = dev_in[n_req:n_req + n_table].view(case.block_table.shape)
-        tokens = dev_in[n_req + n_table:].view(batch, width)
-        lanes.append((torch.cuda.Stream(device=dev), dev_in, req, table, tokens, out, counts,
-                      host_out, host_counts))
+    h2d = d2h = 0
+    for lane_index in range(2):
+        stream = torch.cuda.Stream(device=dev)
+        jobs = []
+        for case in cases:
+            batch, width = case.tokens.shape
+            n_req, n_table = case.req_ids.size, case.block_table.size
+            n_in = n_req + n_table + case.tokens.size
+            host_in = torch.empty(n_in, dtype=torch.int32).pin_memory()
+            host_in[:n_req] = torch.as_tensor(case.req_ids)
+            host_in[n_req:n_req + n_table] = torch.as_tensor(case.block_table.ravel())
+            host_in[n_req + n_table:] = torch.as_tensor(case.tokens.ravel())
+            # Inputs share one device buffer (one H2D copy); the two outputs must
+            # not share storage, so they come back in two D2H copies.
+            dev_in = torch.empty(n_in, dtype=torch.int32, device=dev)
+            bufs = {
+                "req": dev_in[:n_req],
+                "table": dev_in[n_req:n_req + n_table].view(case.block_table.shape),
+                "tokens": dev_in[n_req + n_table:].view(batch, width),
+                "out": torch.empty((batch, width), dtype=torch.int32, device=dev),
+                "counts": torch.empty(batch, dtype=torch.int32, device=dev),
+            }
+            if arm == "hierarchical_stable":
+                # The hierarchical entry point wants every buffer in its own
+                # storage: the inputs land in one staging buffer and are split
+                # into their own tensors on the device.
+                bufs["req"] = torch.empty(n_req, dtype=torch.int32, device=dev)
+                bufs["table"] = torch.empty(case.block_table.shape, dtype=torch.int32, device=dev)
+                bufs["tokens"] = torch.empty((batch, width), dtype=torch.int32, device=dev)
+                bufs["staging"] = dev_in
+                for name, shape in workspace_shapes(batch, width, tile_size=case.tile_size).items():
+                    bufs[name] = torch.empty(shape, dtype=torch.int32, device=dev)
+            host_out = torch.empty((batch, width), dtype=torch.int32).pin_memory()
+            host_counts = torch.empty(batch, dtype=torch.int32).pin_memory()
+            jobs.append((host_in, dev_in, bufs, host_out, host_counts,
+                         _make_call(arm, bufs, case.geometry(), case.tile_size)))
+            if lane_index == 0:
+                h2d += 4 * n_in
+                d2h += 4 * (batch * width + batch)
+        lanes.append((stream, jobs))
 
     def step(i: int) -> None:
-        stream, dev_in, req, table, tokens, out, counts, host_out, host_counts = lanes[i % 2]
+        stream, jobs = lanes[i % 2]
         with torch.cuda.stream(stream):
-            dev_in.copy_(host_in, non_blocking=True)
-            localize_rowwise(req, table, tokens, out, counts, **geometry)
-            host_out.copy_(out, non_blocking=True)
-            host_counts.copy_(counts, non_blocking=True)
+            for host_in, dev_in, bufs, host_out, host_counts, call in jobs:
+                dev_in.copy_(host_in, non_blocking=True)
+                if "staging" in bufs:
+                    n_req, n_table = bufs["req"].numel(), bufs["table"].numel()
+                    bufs["req"].copy_(dev_in[:n_req])
+                    bufs["table"].view(-1).copy_(dev_in[n_req:n_req + n_table])
+                    bufs["tokens"].view(-1).copy_(dev_in[n_req + n_table:])
+                call()
+                host_out.copy_(bufs["out"], non_blocking=True)
+                host_counts.copy_(bufs["counts"], non_blocking=True)
 
-    for i in range(max(3, args.warmup)):
+    for i in range(max(3, min(args.warmup, 8))):
         step(i)
     torch.cuda.synchronize(dev)
     if dist is not None:
@@ -435,12 +517,12 @@ def run_e2e(args, case, dev, geometry, dist) -> dict:
     current = torch.cuda.current_stream(dev)
     current.synchronize()
     start.record(current)
-    for lane in lanes:
-        lane[0].wait_event(start)
+    for stream, _ in lanes:
+        stream.wait_event(start)
     for i in range(steps):
         step(i)
-    for lane in lanes:
-        current.wait_stream(lane[0])
+    for stream, _ in lanes:
+        current.wait_stream(stream)
     end.record(current)
     torch.cuda.synchronize(dev)
     if dist is not None:
@@ -448,14 +530,15 @@ def run_e2e(args, case, dev, geometry, dist) -> dict:
     elapsed_ms = reduce_max(dist, start.elapsed_time(end))
     world = dist.get_world_size() if dist is not None else 1
     per_step = elapsed_ms / 1e3 / steps
+    indices = len(cases) * cases[0].batch * cases[0].width
     return {
-        "value": world * batch * width / per_step / 1e9,
+        "value": world * indices / per_step / 1e9,
         "unit": UNIT,
-        "h2d_bytes_per_step": 4 * n_in,
-        "d2h_bytes_per_step": 4 * (batch * width + batch),
+        "h2d_bytes_per_step": h2d,
+        "d2h_bytes_per_step": d2h,
         "steps": steps,
         "us_per_step": per_step * 1e6,
-        "path": "silkern_b200.localize_rowwise on 2 streams, pinned host buffers",
+        "path": "silkern_b200 public launchers on 2 alternating streams, pinned host buffers",
     }
 
 
@@ -465,6 +548,7 @@ def main(argv=None) -> int:
     parser.add_argument("--steps", type=int, default=2000)
     parser.add_argument("--warmup", type=int, default=64)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=3)
     parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args(argv)

@@ -664,11 +664,14 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
     if (cluster_req > 0) {
       cs = cluster_req;
     } else {
-      // Row-wise: split long rows across a cluster only when there are too
-      // few rows to occupy the SMs.
+      // Row-wise: rows up to 8192 columns stay on one CTA (row groups keep
+      // the SMs balanced and a cluster exchange costs more than it saves);
+      // longer rows are split over a cluster when there are few of them.
       const int sms = sm_count();
       cs = 1;
-      while (cs < kMaxCluster && r.batch * cs * 2 <= sms && width / (2 * cs) >= 1024) cs *= 2;
+      while (width > 8192 && cs < kMaxCluster && r.batch * cs * 2 <= sms && width / (2 * cs) >= 2048) {
+        cs *= 2;
+      }
     }
     slice = (width + cs - 1) / cs;
     slice = (slice + 3) / 4 * 4;
