@@ -27,7 +27,9 @@ compared with the oracle (``bit_exact``).
 
 ``--impl reference`` times the reference algorithm on the host instead: the C
 restatement of the reference's ``localize_reference`` (oracle/) with every
-host thread, on the same workload (rank 0 only).
+host thread, on the same workload (rank 0 only). ``--impl triton`` times the
+reference's own Triton launchers on this GPU when the reference package is
+present under baseline/_ref (a comparison arm; not part of the product).
 """
 
 from __future__ import annotations
@@ -285,6 +287,168 @@ def run_reference(args, rank: int, world: int) -> dict | None:
                       "silkern/contract.py:67-158 in oracle/localize_oracle.c)",
         },
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def _reference_hierarchical_direct(ref_silkern, b: dict, g: dict, tile_size: int) -> None:
+    """The reference's hierarchical Triton kernels, launched as its launcher does.
+
+    Launch parameters of the reference's silkern/kernels.py:560-633, for widths
+    and tile sizes its workspace checks reject.
+    """
+    import triton
+
+    k = ref_silkern.kernels
+    tokens, out = b["tokens"], b["out"]
+    batch, width = tokens.shape
+    tiles = b["tile_counts"].shape[1]
+    compact = g["dcp_size"] > 1
+    k._map_tiles_kernel[(batch, tiles)](
+        b["req"], b["table"], tokens, out, b["mapped"], b["local_positions"], b["tile_counts"],
+        b["table"].stride(0), b["table"].stride(1), tokens.stride(0), tokens.stride(1),
+        out.stride(0), out.stride(1), b["mapped"].stride(0), b["mapped"].stride(1),
+        b["local_positions"].stride(0), b["local_positions"].stride(1),
+        b["tile_counts"].stride(0), b["tile_counts"].stride(1),
+        WIDTH=width, BLOCK_TABLE_WIDTH=b["table"].shape[1], BLOCK_SIZE=g["block_size"],
+        DCP_SIZE=g["dcp_size"], DCP_RANK=g["dcp_rank"], DCP_INTERLEAVE=g["dcp_interleave"],
+        TILE_SIZE=tile_size, DIRECT_OUTPUT=not compact, num_warps=4)
+    k._tile_prefix_kernel[(batch,)](
+        b["tile_counts"], b["tile_offsets"], b["counts"], b["tile_counts"].stride(0),
+        b["tile_counts"].stride(1), b["tile_offsets"].stride(0), b["tile_offsets"].stride(1),
+        NUM_TILES=tiles, PADDED_TILES=triton.next_power_of_2(tiles), num_warps=1)
+    if compact:
+        elements = batch * width
+        k._fill_output_kernel[(triton.cdiv(elements, 256),)](out, elements, BLOCK=256, num_warps=4)
+        k._scatter_tiles_kernel[(batch, tiles)](
+            out, b["mapped"], b["local_positions"], b["tile_counts"], b["tile_offsets"],
+            out.stride(0), out.stride(1), b["mapped"].stride(0), b["mapped"].stride(1),
+            b["local_positions"].stride(0), b["local_positions"].stride(1),
+            b["tile_counts"].stride(0), b["tile_counts"].stride(1), b["tile_offsets"].stride(0),
+            b["tile_offsets"].stride(1), WIDTH=width, TILE_SIZE=tile_size, num_warps=4)
+
+
+def run_triton(args, rank: int, world: int) -> dict | None:
+    """The reference's own Triton launchers on this GPU, timed like our arm.
+
+    Needs the reference package under baseline/_ref (not part of this
+    repository); prints an ``unavailable`` line otherwise. Same workload,
+    buffer rotation and graph-replay timing as ``run_ours``; outputs are
+    checked against the oracle.
+    """
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref_dir, "silkern", "kernels.py")):
+        return {"impl": "triton-reference", "unavailable": "reference package not installed in baseline/_ref"}
+    if rank != 0:
+        return None
+    import numpy as np
+    import torch
+
+    import oracle
+
+    sys.path.insert(0, ref_dir)
+    for name in [m for m in sys.modules if m == "silkern" or m.startswith("silkern.")]:
+        del sys.modules[name]
+    import silkern as ref_silkern  # the reference implementation
+
+    if not os.path.abspath(ref_silkern.__file__).startswith(ref_dir):
+        return {"impl": "triton-reference", "unavailable": "could not import the reference package"}
+    config = args.config
+    spec = WORKLOADS[config]
+    calls = spec["calls"]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    distinct = calls if calls > 1 else DISTINCT_CASES
+    cases = [_case(config, seed=1000 + i, dcp_rank=0) for i in range(distinct)]
+    direct = spec["arm"] == "hierarchical_stable" and (
+        cases[0].width > ref_silkern.MAX_ROW_WIDTH or cases[0].tile_size not in ref_silkern.SUPPORTED_TILE_SIZES)
+    bytes_per_call = cases[0].algorithmic_bytes()
+    n_sets = max(64, math.ceil(2.05 * L2_BYTES / bytes_per_call))
+    n_sets = math.ceil(n_sets / distinct) * distinct
+    sets = []
+    for i in range(n_sets):
+        case = cases[i % distinct]
+        bufs = {name: torch.as_tensor(a).to(dev) for name, a in
+                (("req", case.req_ids), ("table", case.block_table), ("tokens", case.tokens))}
+        bufs["out"] = torch.empty_like(bufs["tokens"])
+        bufs["counts"] = torch.empty(case.batch, dtype=torch.int32, device=dev)
+        geometry = case.geometry()
+        if spec["arm"] == "row_stable":
+            call = (lambda b=bufs, g=geometry: ref_silkern.localize_rowwise(
+                b["req"], b["table"], b["tokens"], b["out"], b["counts"], **g))
+        else:
+            tiles = (case.width + case.tile_size - 1) // case.tile_size
+            for name, shape in (("mapped", (case.batch, case.width)), ("local_positions", (case.batch, case.width)),
+                                ("tile_counts", (case.batch, tiles)), ("tile_offsets", (case.batch, tiles))):
+                bufs[name] = torch.empty(shape, dtype=torch.int32, device=dev)
+            if direct:
+                # The reference launcher rejects this width/tile (its workspace
+                # limits), so its four Triton kernels are launched directly with
+                # the launcher's own parameters.
+                call = (lambda b=bufs, g=geometry, t=case.tile_size: _reference_hierarchical_direct(
+                    ref_silkern, b, g, t))
+            else:
+                call = (lambda b=bufs, g=geometry, t=case.tile_size: ref_silkern.localize_hierarchical(
+                    b["req"], b["table"], b["tokens"], b["out"], b["counts"], b["mapped"],
+                    b["local_positions"], b["tile_counts"], b["tile_offsets"], tile_size=t, **g))
+        sets.append((bufs, call))
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for i in range(n_sets):
+            sets[i][1]()
+    torch.cuda.synchronize(dev)
+
+    def plan_graphs(first: int, count: int):
+        graphs = []
+        done = 0
+        while done < count:
+            n = min(CHUNK, count - done)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(first + done, first + done + n):
+                    sets[i % n_sets][1]()
+            graphs.append(graph)
+            done += n
+        return graphs
+
+    warm = plan_graphs(0, args.warmup * calls)
+    main_graphs = plan_graphs(args.warmup * calls, args.steps * calls)
+    with torch.cuda.stream(stream):
+        for g in warm:
+            g.replay()
+    torch.cuda.synchronize(dev)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(200_000)
+        start.record(stream)
+        for g in main_graphs:
+            g.replay()
+        end.record(stream)
+    torch.cuda.synchronize(dev)
+    per_step_s = start.elapsed_time(end) / 1e3 / args.steps
+    per_call_s = per_step_s / calls
+    expected = [oracle.localize(c.req_ids, c.block_table, c.tokens, threads=4, **c.geometry()) for c in cases]
+    bit_exact = all(
+        np.array_equal(sets[i][0]["out"].cpu().numpy(), expected[i % distinct][0])
+        and np.array_equal(sets[i][0]["counts"].cpu().numpy(), expected[i % distinct][1])
+        for i in range(n_sets))
+    peaks = _peaks()
+    achieved = bytes_per_call / per_call_s / 1e9
+    return {
+        "impl": "triton-reference",
+        "metric": METRIC if config == 3 else f"Gindices/s per B200, config {config}",
+        "value": calls * cases[0].batch * cases[0].width / per_step_s / 1e9,
+        "unit": UNIT,
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "us_per_call": per_call_s * 1e6,
+        "bit_exact": bit_exact,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"]},
+        "config": _workload_config(config, 1, n_sets),
+        "source": "reference silkern.localize_rowwise / localize_hierarchical (Triton) from baseline/_ref",
     }
 
 
@@ -547,7 +711,7 @@ def main(argv=None) -> int:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=2000)
     parser.add_argument("--warmup", type=int, default=64)
-    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--impl", choices=["ours", "reference", "triton"], default="ours")
     parser.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=3)
     parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -559,8 +723,8 @@ def main(argv=None) -> int:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
-    if args.impl == "reference":
-        result = run_reference(args, rank, world)
+    if args.impl in ("reference", "triton"):
+        result = (run_reference if args.impl == "reference" else run_triton)(args, rank, world)
         if result is not None:
             print(json.dumps(result), flush=True)
         return 0

@@ -483,3 +483,22 @@ def test_decode_step_of_48_layers_in_one_graph(golden) -> None:
     assert torch.cuda.memory_allocated() == allocated
     for (*_, out, counts), layer in zip(bufs, range(48), strict=True):
         assert digest(out.cpu().numpy(), counts.cpu().numpy()) == expected[5000 + layer]
+
+
+@pytest.mark.parametrize("width", [4, 100, 512, 2048, 6000])
+@pytest.mark.parametrize("batch", [1, 147, 148, 149, 296, 297, 1000, 3000])
+def test_row_groups_over_batch_sizes(width, batch) -> None:
+    """Row-wise CTAs pack several rows (up to 1024 threads) and spread the batch
+    over at most one CTA per SM; every batch/width split must stay exact."""
+    if batch * width > 4_000_000:
+        pytest.skip("large case covered by the full-size tests")
+    rng = np.random.default_rng(batch * 7 + width)
+    tokens = rng.integers(-5, 64 * 40 * 4, size=(batch, width), dtype=np.int32)
+    table = rng.integers(-2, 50000, size=(37, 40), dtype=np.int32)
+    req = rng.integers(0, 37, size=batch, dtype=np.int32)
+    for kw in (dict(block_size=64, dcp_size=4, dcp_rank=3), dict(block_size=48, dcp_size=3, dcp_rank=1),
+               dict(block_size=64, dcp_size=1, dcp_rank=0)):
+        want = _oracle(req, table, tokens, **kw)
+        out, counts = run_rowwise(req, table, tokens, **kw)
+        assert np.array_equal(out, want[0]), kw
+        assert np.array_equal(counts, want[1]), kw
