@@ -335,6 +335,25 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
     }
   }
 
+  // Hierarchical: the CTA-local exclusive position of the element in each
+  // tile's first column is that tile's offset (before the row offset), staged
+  // in shared memory ahead of the barrier that publishes the survivors.
+  int32_t* s_tile = gsmem + p.smem_tile;
+  const bool tiles = p.tile_shift >= 0;
+  if (tiles) {
+    const int tmask = (1 << p.tile_shift) - 1;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int col = 4 * (i * nthreads + tid);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (col + j < len && ((col + j) & tmask) == 0) {
+          s_tile[(col + j) >> p.tile_shift] = base[i] + lane_pre[i] + __popc(bits[i] & ((1u << j) - 1u));
+        }
+      }
+    }
+  }
+
   int32_t* orow = p.out + row * p.width;
   if constexpr (COMPACT) {
     // Stage this CTA's survivors compactly in shared memory, then write them
@@ -383,6 +402,7 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
       }
     }
   } else {
+    if (tiles) __syncthreads();  // the compacting path's staging barrier covers s_tile
     int32_t* dst = orow + c0;
     const bool out_vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
 #pragma unroll
@@ -399,30 +419,14 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
     }
   }
 
-  if (p.tile_shift >= 0) {
-    // Publish the tile decomposition: the exclusive position of the element
-    // in a tile's first column is that tile's offset; counts are differences.
-    int32_t* s_tile = gsmem + p.smem_tile;
-    const int tmask = (1 << p.tile_shift) - 1;
-#pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int col = 4 * (i * nthreads + tid);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (col + j < len && ((col + j) & tmask) == 0) {
-          s_tile[(col + j) >> p.tile_shift] =
-              row_off + base[i] + lane_pre[i] + __popc(bits[i] & ((1u << j) - 1u));
-        }
-      }
-    }
-    __syncthreads();
-    const int ntiles = (len + tmask) >> p.tile_shift;
-    const int cta_end = row_off + cta_total;
+  if (tiles) {
+    // Offsets and counts (differences of offsets) of this CTA's tiles.
+    const int ntiles = (len + (1 << p.tile_shift) - 1) >> p.tile_shift;
     const int64_t tbase = row * p.tiles_per_row + (c0 >> p.tile_shift);
     for (int m = tid; m < ntiles; m += nthreads) {
       const int o = s_tile[m];
-      const int next = m + 1 < ntiles ? s_tile[m + 1] : cta_end;
-      p.tile_offsets[tbase + m] = o;
+      const int next = m + 1 < ntiles ? s_tile[m + 1] : cta_total;
+      p.tile_offsets[tbase + m] = row_off + o;
       p.tile_counts[tbase + m] = next - o;
     }
   }
@@ -646,14 +650,19 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
   int cs;
   int slice;
   if (r.tile_size != 0) {
-    // Hierarchical: a CTA covers a whole number of tiles, at most 8 CTAs per
-    // row, and (unless the row is shorter) at least 1024 columns.
+    // Hierarchical: a CTA covers a whole number of tiles; the cluster is the
+    // largest power of two (up to 8) that keeps batch x cluster within about
+    // one CTA per SM, and (unless the row is shorter) a CTA covers at least
+    // 1024 columns.
     const int tiles = (width + r.tile_size - 1) / r.tile_size;
     int per_cta;
     if (cluster_req > 0) {
       per_cta = (tiles + cluster_req - 1) / cluster_req;
     } else {
-      per_cta = (tiles + kMaxCluster - 1) / kMaxCluster;
+      const int sms = sm_count();
+      int cs_target = 1;
+      while (cs_target < kMaxCluster && r.batch * cs_target * 2 <= sms) cs_target *= 2;
+      per_cta = (tiles + cs_target - 1) / cs_target;
       const int min_tiles = (1024 + r.tile_size - 1) / r.tile_size;
       if (per_cta < min_tiles) per_cta = min_tiles;
       if (per_cta > tiles) per_cta = tiles;
