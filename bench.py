@@ -80,7 +80,7 @@ def _peaks() -> dict:
 
 def _traffic(config: int) -> dict | None:
     """DRAM bytes per launch from the committed ncu summary of this workload, if any."""
-    name = WORKLOADS[config]["arm"].replace("_stable", "")
+    name = {"row_stable": "rowwise", "hierarchical_stable": "hierarchical"}[WORKLOADS[config]["arm"]]
     path = os.path.join(REPO, "profiles", f"localize_{name}_config{config}.md")
     try:
         with open(path) as fh:
