@@ -42,6 +42,7 @@ namespace silkern {
 
 constexpr int kMaxThreads = 512;      // threads per row group
 constexpr int kMaxCtaThreads = 1024;  // threads per CTA (row groups of one-chunk rows)
+constexpr int kMaxRowGroups = 15;     // row groups per CTA: named barriers 1..15
 constexpr int kMaxCluster = 8;
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
 constexpr uint32_t kFull = 0xffffffffu;
@@ -100,6 +101,14 @@ __device__ __forceinline__ void fill_invalid(int32_t* row, int lo, int hi, int t
   for (int g = tid; g < nvec; g += nthreads) body[g] = make_int4(-1, -1, -1, -1);
   const int rest = n - head - 4 * nvec;
   if (tid < rest) dst[head + 4 * nvec + tid] = -1;
+}
+
+// Barrier over one row group (threads [group * n, group * n + n) of the CTA),
+// named barrier 1 + group: for a branch that is uniform over one row but not
+// over the CTA. Barriers every row group reaches stay CTA-wide
+// (__syncthreads measured faster than per-group barriers).
+__device__ __forceinline__ void group_sync(int group, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(group + 1), "r"(nthreads) : "memory");
 }
 
 // dst[0:n] = src[0:n] (src in shared memory) with 128-bit stores on the
@@ -234,12 +243,12 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
   }
   const int32_t* trow = p.table + static_cast<int64_t>(req_ok ? req : 0) * p.table_width;
   if constexpr (STAGE) {
-    if (req_ok && static_cast<int64_t>(req) != row) {  // the same for every thread of the CTA
+    if (req_ok && static_cast<int64_t>(req) != row) {  // the same for every thread of the row group
       // Every thread's speculative copies must land before any repair copy
       // is issued: the two rows can differ in 16-byte alignment, and then the
       // two passes split the entries between threads differently.
       cp_async_wait_all();
-      __syncthreads();
+      group_sync(group, nthreads);
       stage_row_async(s_tbl, trow, static_cast<int>(p.table_width), tid, nthreads);
     }
     cp_async_wait_all();
@@ -699,7 +708,8 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
     // CTA per SM.
     g->threads = static_cast<int>(next_pow2(static_cast<uint32_t>(g->threads)));
     if (g->nc == 1) {
-      const int64_t max_rows = kMaxCtaThreads / g->threads;
+      int64_t max_rows = kMaxCtaThreads / g->threads;
+      if (max_rows > kMaxRowGroups) max_rows = kMaxRowGroups;
       int64_t ctas = r.batch < sm_count() ? r.batch : sm_count();
       int64_t rows = (r.batch + ctas - 1) / ctas;
       if (rows > max_rows) {

@@ -502,3 +502,22 @@ def test_row_groups_over_batch_sizes(width, batch) -> None:
         out, counts = run_rowwise(req, table, tokens, **kw)
         assert np.array_equal(out, want[0]), kw
         assert np.array_equal(counts, want[1]), kw
+
+
+@pytest.mark.parametrize("batch", [40, 300, 1000])
+def test_staged_table_with_packed_rows_and_mixed_speculation(batch) -> None:
+    """Several rows share a CTA; some rows' request is their own index (the
+    staged copy is right), others' is not (the copy is repaired). Each row
+    synchronises only its own group, so the mix must stay exact."""
+    rng = np.random.default_rng(batch + 99)
+    width = 512
+    table = rng.integers(-2, 70000, size=(batch + 5, 40), dtype=np.int32)
+    tokens = rng.integers(-5, 64 * 40 * 4, size=(batch, width), dtype=np.int32)
+    req = np.arange(batch, dtype=np.int32)
+    flip = rng.random(batch) < 0.5
+    req[flip] = rng.integers(0, batch + 5, size=int(flip.sum()), dtype=np.int32)
+    kw = dict(block_size=64, dcp_size=4, dcp_rank=2)
+    want = _oracle(req, table, tokens, **kw)
+    for prefetch in (0, 1):
+        out, counts, _ = _explicit(req, table, tokens, cluster=1, stage=1, prefetch=prefetch, **kw)
+        assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
