@@ -138,7 +138,7 @@ def _oracle(req, table, tokens, **kw):
     return oracle.localize(req, table, tokens, threads=4, **kw)
 
 
-def _explicit(req, table, tokens, *, cluster, stage, prefetch, tile_size=0, **kw):
+def _explicit(req, table, tokens, *, cluster, stage, prefetch, tile_size=0, status=None, **kw):
     req, table, tokens = (_cuda(a) for a in (req, table, tokens))
     batch, width = tokens.shape
     out = torch.full_like(tokens, 0x5A5A5A5A)
@@ -150,7 +150,7 @@ def _explicit(req, table, tokens, *, cluster, stage, prefetch, tile_size=0, **kw
         to = torch.empty((batch, tiles), dtype=torch.int32, device=DEV)
     localize_explicit(req, table, tokens, out, counts, cluster_size=cluster, stage_table=stage,
                       prefetch_table=prefetch, tile_size=tile_size, tile_counts=tc,
-                      tile_offsets=to, **kw)
+                      tile_offsets=to, status=status, **kw)
     torch.cuda.synchronize()
     tiles_out = None if tc is None else (tc.cpu().numpy(), to.cpu().numpy())
     return out.cpu().numpy(), counts.cpu().numpy(), tiles_out
@@ -521,3 +521,36 @@ def test_staged_table_with_packed_rows_and_mixed_speculation(batch) -> None:
     for prefetch in (0, 1):
         out, counts, _ = _explicit(req, table, tokens, cluster=1, stage=1, prefetch=prefetch, **kw)
         assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
+
+
+@pytest.mark.parametrize("cluster", [2, 4, 8])
+@pytest.mark.parametrize("tile_size", [0, 128])
+def test_cluster_noncompacting_and_bad_requests(cluster, tile_size) -> None:
+    """Split rows without compaction (columns keep their values) and rows whose
+    request id is outside the table, on every cluster size."""
+    rng = np.random.default_rng(cluster * 10 + tile_size)
+    batch, width = 6, 4000
+    tokens = rng.integers(-3, 64 * 30 * 2, size=(batch, width), dtype=np.int32)
+    table = rng.integers(-2, 9000, size=(4, 30), dtype=np.int32)
+    req = np.array([0, 3, 1, 2, 1, 0], dtype=np.int32)
+    for compact in (False, True):
+        kw = dict(block_size=64, dcp_size=2, dcp_rank=1, compact_valid_to_front=compact)
+        want = _oracle(req, table, tokens, **kw)
+        out, counts, tiles = _explicit(req, table, tokens, cluster=cluster, stage=0, prefetch=1,
+                                       tile_size=tile_size, **kw)
+        assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
+        if tile_size:
+            wt = oracle.tiles(req, table, tokens, tile_size=tile_size, block_size=64, dcp_size=2, dcp_rank=1)
+            assert np.array_equal(tiles[0], wt[0]) and np.array_equal(tiles[1], wt[1])
+    # request ids outside the table: those rows come out empty, the others exact
+    bad = req.copy()
+    bad[[1, 4]] = [7, -2]
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kw = dict(block_size=64, dcp_size=2, dcp_rank=1)
+    out, counts, _ = _explicit(bad, table, tokens, cluster=cluster, stage=0, prefetch=1,
+                               tile_size=tile_size, status=status, **kw)
+    good = np.array([0, 2, 3, 5])
+    want = _oracle(bad[good], table, tokens[good], **kw)
+    assert np.array_equal(out[good], want[0]) and np.array_equal(counts[good], want[1])
+    assert np.all(out[[1, 4]] == -1) and np.all(counts[[1, 4]] == 0)
+    assert int(status.item()) == 1
