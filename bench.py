@@ -453,8 +453,12 @@ def run_triton(args, rank: int, world: int) -> dict | None:
 
 
 def _make_call(arm: str, bufs: dict, geometry: dict, tile_size: int):
+    from silkern_b200.baselines import launch_atomic_baseline
     from silkern_b200.kernels import localize_hierarchical, localize_rowwise
 
+    if arm == "atomic":
+        return lambda: launch_atomic_baseline(bufs["req"], bufs["table"], bufs["tokens"], bufs["out"],
+                                              bufs["counts"], bufs["scratch"], **geometry)
     if arm == "row_stable":
         return lambda: localize_rowwise(bufs["req"], bufs["table"], bufs["tokens"], bufs["out"],
                                         bufs["counts"], **geometry)
@@ -473,7 +477,9 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     from silkern_b200.workspace import workspace_shapes
 
     config = args.config
-    spec = WORKLOADS[config]
+    spec = dict(WORKLOADS[config])
+    if args.impl == "atomic":
+        spec["arm"] = "atomic"
     calls = spec["calls"]
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -494,6 +500,8 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
         if spec["arm"] == "hierarchical_stable":
             for name, shape in workspace_shapes(case.batch, case.width, tile_size=case.tile_size).items():
                 bufs[name] = torch.empty(shape, dtype=torch.int32, device=dev)
+        if spec["arm"] == "atomic":
+            bufs["scratch"] = torch.empty(case.batch, dtype=torch.int32, device=dev)
         sets.append((bufs, _make_call(spec["arm"], bufs, case.geometry(), case.tile_size)))
     indices_per_call = cases[0].batch * cases[0].width
 
@@ -558,17 +566,22 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     for index in sorted(used):
         bufs = sets[index][0]
         want_out, want_counts = expected[index % distinct]
-        if not (np.array_equal(bufs["out"].cpu().numpy(), want_out)
+        got_out = bufs["out"].cpu().numpy()
+        if spec["arm"] == "atomic":  # same set and count; the order is unspecified
+            got_out = np.sort(np.where(got_out < 0, np.iinfo(np.int32).max, got_out), axis=1)
+            want_out = np.sort(np.where(want_out < 0, np.iinfo(np.int32).max, want_out), axis=1)
+        if not (np.array_equal(got_out, want_out)
                 and np.array_equal(bufs["counts"].cpu().numpy(), want_counts)):
             bit_exact = False
     del warm_graphs, main_graphs
 
-    e2e = run_e2e(args, cases[:calls], dev, dist)
+    e2e = run_e2e(args, cases[:calls], dev, dist) if args.impl == "ours" else None
 
     peaks = _peaks()
     achieved = bytes_per_call / per_call_s / 1e9
     traffic = _traffic(config)
     result = {
+        **({"impl": "atomic-baseline"} if args.impl == "atomic" else {}),
         "metric": METRIC if config == 3 else f"Gindices/s per B200, config {config}",
         "value": world * calls * indices_per_call / per_step_s / 1e9,
         "unit": UNIT,
@@ -711,7 +724,7 @@ def main(argv=None) -> int:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=2000)
     parser.add_argument("--warmup", type=int, default=64)
-    parser.add_argument("--impl", choices=["ours", "reference", "triton"], default="ours")
+    parser.add_argument("--impl", choices=["ours", "reference", "triton", "atomic"], default="ours")
     parser.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=3)
     parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -738,7 +751,7 @@ def main(argv=None) -> int:
         torch_dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
         dist = torch_dist
     try:
-        result = run_ours(args, rank, world, local_rank, dist)
+        result = run_ours(args, rank, world, local_rank, dist)  # also --impl atomic
     finally:
         if dist is not None:
             dist.destroy_process_group()

@@ -171,6 +171,21 @@ int silkern_localize_hierarchical_noalloc_v1(const int32_t* req_ids, const int32
 int silkern_count_mismatches_v1(const int32_t* a, const int32_t* b, int64_t n,
                                 int32_t* mismatches, void* stream);
 
+/*
+ * Comparison baseline, not the product: the atomic-reservation converter of
+ * the reference's bench/atomic_baseline.py:40-111 and :313-385 (itself a
+ * restatement of the upstream vLLM converter). Same set and counts as the
+ * entry points above, but each 128-column tile reserves its output segment
+ * with an atomicAdd on scratch[row] (int32, (batch,)), so the order of the
+ * segments varies from run to run. Three stream operations: reset, reserve
+ * and scatter, counts <- scratch.
+ */
+int silkern_atomic_baseline_v1(const int32_t* req_ids, const int32_t* block_table,
+                               int64_t table_rows, int64_t table_width, const int32_t* tokens,
+                               int32_t* out, int32_t* counts, int32_t* scratch, int64_t batch,
+                               int64_t width, int32_t block_size, int32_t dcp_size,
+                               int32_t dcp_rank, int32_t dcp_interleave, void* stream);
+
 /* Static text for a return code (positive SILKERN_E*, 0, or -cudaError_t). */
 const char* silkern_status_string_v1(int code);
 
