@@ -350,16 +350,13 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
   int32_t* s_tile = gsmem + p.smem_tile;
   const bool tiles = p.tile_shift >= 0;
   if (tiles) {
+    // Tiles are multiples of 64 columns and chunks start at multiples of 4,
+    // so a tile can only start at a chunk's first column (prefix 0 in-lane).
     const int tmask = (1 << p.tile_shift) - 1;
 #pragma unroll
     for (int i = 0; i < NC; ++i) {
       const int col = 4 * (i * nthreads + tid);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (col + j < len && ((col + j) & tmask) == 0) {
-          s_tile[(col + j) >> p.tile_shift] = base[i] + lane_pre[i] + __popc(bits[i] & ((1u << j) - 1u));
-        }
-      }
+      if (col < len && (col & tmask) == 0) s_tile[col >> p.tile_shift] = base[i] + lane_pre[i];
     }
   }
 
@@ -634,18 +631,22 @@ void smem_limits(int* per_sm, int* reserved) {
   *reserved = cache_res[dev];
 }
 
-// Chunks of four columns per thread and threads per CTA for `slice` columns:
-// up to kMaxThreads threads with one chunk each, then more chunks per thread
-// (short per-thread dependency chains measured faster than fewer, longer ones).
-bool fit_slice(int slice, int nc_req, int* nc, int* threads) {
+// Chunks of four columns per thread and threads for `slice` columns: up to
+// max_threads threads with one chunk each, then more chunks per thread over
+// at most kMaxThreads threads (short per-thread dependency chains measured
+// faster than fewer, longer ones).
+bool fit_slice(int slice, int nc_req, int max_threads, int* nc, int* threads) {
   const int granules = (slice + 3) / 4;
   int c = 1;
   if (nc_req > 0) {
     c = nc_req;
-  } else {
+  } else if (granules > max_threads) {
+    // more than one chunk per thread: groups of at most kMaxThreads
+    c = 2;
     while (granules > c * kMaxThreads) c *= 2;
   }
-  if (c > 8 || granules > c * kMaxThreads) return false;
+  const int limit = c == 1 ? max_threads : kMaxThreads;
+  if (c > 8 || granules > c * limit) return false;
   int t = (granules + c - 1) / c;
   t = (t + 31) / 32 * 32;
   *nc = c;
@@ -697,7 +698,10 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
   }
   if (cluster_req > 0 && cs != cluster_req) return SILKERN_E_GEOMETRY;
   if (cs < 1 || cs > kMaxCluster) return SILKERN_E_GEOMETRY;
-  if (!fit_slice(slice, nc_req, &g->nc, &g->threads)) return SILKERN_E_GEOMETRY;
+  // A cluster CTA or a row group has at most kMaxThreads threads (cluster
+  // CTAs of 1024 threads under a 32-register bound measured slower); short
+  // rows share a CTA (row groups, below).
+  if (!fit_slice(slice, nc_req, kMaxThreads, &g->nc, &g->threads)) return SILKERN_E_GEOMETRY;
   g->cluster = cs;
   g->slice = slice;
   g->rows_per_cta = 1;
