@@ -155,3 +155,25 @@ def test_explicit_rejects_bad_geometry(lib) -> None:
     assert call(8, width=16) == 7  # 8 CTAs cannot each own 4-column slices of 16 columns
     assert call(1, chunks=3) == 7
     assert call(1, chunks=1, width=16384) == 7  # 4096 granules do not fit 512 threads x 1 chunk
+
+
+def test_missing_library_fails_loudly(tmp_path) -> None:
+    """No CPU or Triton fallback: without the library every launcher raises."""
+    import subprocess
+    import sys
+
+    code = (
+        "import sys; sys.path.insert(0, %r)\n"
+        "import silkern_b200._native as nat\n"
+        "nat.LIB_PATH = %r\n"
+        "from silkern_b200 import LocalizationError\n"
+        "try:\n"
+        "    nat.load()\n"
+        "except LocalizationError as exc:\n"
+        "    print('raised:', exc)\n"
+        "else:\n"
+        "    print('loaded')\n"
+    ) % (REPO, str(tmp_path / "missing.so"))
+    proc = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert proc.returncode == 0, proc.stderr
+    assert proc.stdout.startswith("raised:") and "not built" in proc.stdout
