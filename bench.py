@@ -1,6 +1,7 @@
 """Benchmark of the localization converter on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton|vllm|atomic]
+                    [--config C]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
 
 Default workload (config 3, one step = one converter call): a selection batch
@@ -30,6 +31,8 @@ restatement of the reference's ``localize_reference`` (oracle/) with every
 host thread, on the same workload (rank 0 only). ``--impl triton`` times the
 reference's own Triton launchers on this GPU when the reference package is
 present under baseline/_ref (a comparison arm; not part of the product).
+``--impl vllm`` times vLLM's own non-DCP converter beside ours on the
+workload's shapes at dcp_size 1, where the two compute the same function.
 """
 
 from __future__ import annotations
@@ -327,6 +330,46 @@ def _reference_hierarchical_direct(ref_silkern, b: dict, g: dict, tile_size: int
             b["tile_offsets"].stride(1), WIDTH=width, TILE_SIZE=tile_size, num_warps=4)
 
 
+def _replay_seconds(launch, warm_launches: int, timed_launches: int, stream, dev) -> float:
+    """Device seconds taken by ``timed_launches`` calls replayed from CUDA graphs.
+
+    ``launch(i)`` issues call ``i``. Calls ``0 .. warm_launches-1`` are captured
+    and replayed untimed first; the timed calls follow them, up to CHUNK calls
+    per graph, replayed back to back on ``stream`` between two CUDA events.
+    """
+    import torch
+
+    def plan_graphs(first: int, count: int):
+        graphs = []
+        done = 0
+        while done < count:
+            n = min(CHUNK, count - done)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(first + done, first + done + n):
+                    launch(i)
+            graphs.append(graph)
+            done += n
+        return graphs
+
+    warm = plan_graphs(0, warm_launches)
+    timed = plan_graphs(warm_launches, timed_launches)
+    with torch.cuda.stream(stream):
+        for g in warm:
+            g.replay()
+    torch.cuda.synchronize(dev)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(200_000)  # keep the GPU busy while the replays are queued
+        start.record(stream)
+        for g in timed:
+            g.replay()
+        end.record(stream)
+    torch.cuda.synchronize(dev)
+    return start.elapsed_time(end) / 1e3
+
+
 def run_triton(args, rank: int, world: int) -> dict | None:
     """The reference's own Triton launchers on this GPU, timed like our arm.
 
@@ -397,36 +440,8 @@ def run_triton(args, rank: int, world: int) -> dict | None:
         for i in range(n_sets):
             sets[i][1]()
     torch.cuda.synchronize(dev)
-
-    def plan_graphs(first: int, count: int):
-        graphs = []
-        done = 0
-        while done < count:
-            n = min(CHUNK, count - done)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                for i in range(first + done, first + done + n):
-                    sets[i % n_sets][1]()
-            graphs.append(graph)
-            done += n
-        return graphs
-
-    warm = plan_graphs(0, args.warmup * calls)
-    main_graphs = plan_graphs(args.warmup * calls, args.steps * calls)
-    with torch.cuda.stream(stream):
-        for g in warm:
-            g.replay()
-    torch.cuda.synchronize(dev)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        torch.cuda._sleep(200_000)
-        start.record(stream)
-        for g in main_graphs:
-            g.replay()
-        end.record(stream)
-    torch.cuda.synchronize(dev)
-    per_step_s = start.elapsed_time(end) / 1e3 / args.steps
+    per_step_s = _replay_seconds(lambda i: sets[i % n_sets][1](), args.warmup * calls,
+                                 args.steps * calls, stream, dev) / args.steps
     per_call_s = per_step_s / calls
     expected = [oracle.localize(c.req_ids, c.block_table, c.tokens, threads=4, **c.geometry()) for c in cases]
     bit_exact = all(
@@ -449,6 +464,103 @@ def run_triton(args, rank: int, world: int) -> dict | None:
                      "frac": achieved / peaks["hbm_gbs"]},
         "config": _workload_config(config, 1, n_sets),
         "source": "reference silkern.localize_rowwise / localize_hierarchical (Triton) from baseline/_ref",
+    }
+
+
+def run_vllm(args, rank: int, world: int) -> dict | None:
+    """vLLM's own sparse index converter beside ours, both at ``dcp_size`` 1.
+
+    ``vllm.v1.attention.backends.mla.sparse_utils.triton_convert_req_index_to_global_index``
+    has no DCP split. At ``dcp_size`` 1 it computes the same function as the
+    localizer (every token owned, invalid elements -1 in place, no compaction),
+    so both run on the workload's shapes with ``dcp_size`` set to 1: vLLM's
+    call as its attention backends make it (output and zeroed counts allocated
+    per call, ``return_valid_counts=True``), and ours through the public
+    launcher on caller-owned buffers. Same buffer rotation and graph-replay
+    timing as the other arms; every buffer set's eager output of both is
+    compared with the oracle. A comparison arm, rank 0 only.
+    """
+    if rank != 0:
+        return None
+    try:
+        import vllm
+        from vllm.v1.attention.backends.mla import sparse_utils
+    except Exception as exc:  # noqa: BLE001  (any import failure means no comparison)
+        return {"impl": "vllm-upstream", "unavailable": f"vLLM converter not importable: {exc!r}"[:300]}
+    import dataclasses
+
+    import numpy as np
+    import torch
+
+    import oracle
+    from silkern_b200.workspace import workspace_shapes
+
+    config = args.config
+    spec = WORKLOADS[config]
+    calls = spec["calls"]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    distinct = calls if calls > 1 else DISTINCT_CASES
+    cases = [dataclasses.replace(_case(config, seed=1000 + i, dcp_rank=0), dcp_size=1, dcp_rank=0)
+             for i in range(distinct)]
+    bytes_per_call = cases[0].algorithmic_bytes()
+    n_sets = max(64, math.ceil(2.05 * L2_BYTES / bytes_per_call))
+    n_sets = math.ceil(n_sets / distinct) * distinct
+    sets = []
+    for i in range(n_sets):
+        case = cases[i % distinct]
+        bufs = {name: torch.as_tensor(a).to(dev) for name, a in
+                (("req", case.req_ids), ("table", case.block_table), ("tokens", case.tokens))}
+        bufs["out"] = torch.empty_like(bufs["tokens"])
+        bufs["counts"] = torch.empty(case.batch, dtype=torch.int32, device=dev)
+        if spec["arm"] == "hierarchical_stable":
+            for name, shape in workspace_shapes(case.batch, case.width, tile_size=case.tile_size).items():
+                bufs[name] = torch.empty(shape, dtype=torch.int32, device=dev)
+        sets.append(bufs)
+    geometry = cases[0].geometry()
+    block_size, width = cases[0].block_size, cases[0].width
+
+    def vllm_call(b):
+        return sparse_utils.triton_convert_req_index_to_global_index(
+            b["req"], b["table"], b["tokens"], BLOCK_SIZE=block_size, NUM_TOPK_TOKENS=width,
+            return_valid_counts=True)
+
+    ours = [_make_call(spec["arm"], b, geometry, cases[0].tile_size) for b in sets]
+    expected = [oracle.localize(c.req_ids, c.block_table, c.tokens, threads=4, **c.geometry()) for c in cases]
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    exact = {"vllm": True, "ours": True}
+    with torch.cuda.stream(stream):
+        for i, b in enumerate(sets):
+            want_out, want_counts = expected[i % distinct]
+            got_out, got_counts = vllm_call(b)
+            ours[i]()
+            torch.cuda.synchronize(dev)
+            exact["vllm"] &= (np.array_equal(got_out.cpu().numpy(), want_out)
+                              and np.array_equal(got_counts.cpu().numpy(), want_counts))
+            exact["ours"] &= (np.array_equal(b["out"].cpu().numpy(), want_out)
+                              and np.array_equal(b["counts"].cpu().numpy(), want_counts))
+    warm, timed = args.warmup * calls, args.steps * calls
+    vllm_s = _replay_seconds(lambda i: vllm_call(sets[i % n_sets]), warm, timed, stream, dev)
+    ours_s = _replay_seconds(lambda i: ours[i % n_sets](), warm, timed, stream, dev)
+    indices = cases[0].batch * width
+    return {
+        "impl": "vllm-upstream",
+        "metric": f"Gindices/s per B200, config {config} shapes at dcp_size 1",
+        "value": indices * timed / vllm_s / 1e9,
+        "unit": UNIT,
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "us_per_call": vllm_s / timed * 1e6,
+        "ours_us_per_call": ours_s / timed * 1e6,
+        "ours_value": indices * timed / ours_s / 1e9,
+        "bit_exact": exact,
+        "vllm_version": vllm.__version__,
+        "config": {**_workload_config(config, 1, n_sets), "dcp_size": 1, "dcp_rank": 0},
+        "source": "vllm.v1.attention.backends.mla.sparse_utils.triton_convert_req_index_to_global_index"
+                  " (per-call allocation included) vs silkern_b200 "
+                  + ("localize_rowwise" if spec["arm"] == "row_stable" else "localize_hierarchical"),
     }
 
 
@@ -724,7 +836,7 @@ def main(argv=None) -> int:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=2000)
     parser.add_argument("--warmup", type=int, default=64)
-    parser.add_argument("--impl", choices=["ours", "reference", "triton", "atomic"], default="ours")
+    parser.add_argument("--impl", choices=["ours", "reference", "triton", "vllm", "atomic"], default="ours")
     parser.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=3)
     parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -736,8 +848,9 @@ def main(argv=None) -> int:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
-    if args.impl in ("reference", "triton"):
-        result = (run_reference if args.impl == "reference" else run_triton)(args, rank, world)
+    if args.impl in ("reference", "triton", "vllm"):
+        result = {"reference": run_reference, "triton": run_triton, "vllm": run_vllm}[args.impl](
+            args, rank, world)
         if result is not None:
             print(json.dumps(result), flush=True)
         return 0
