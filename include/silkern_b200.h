@@ -52,6 +52,9 @@ extern "C" {
 #define SILKERN_E_SCRATCH 8      /* batch x tiles exceeds SILKERN_NOALLOC_MAX_TILES */
 
 #define SILKERN_STATUS_BAD_REQUEST 1
+/* Status bits of the fused top-k entry point (OR-ed into *status). */
+#define SILKERN_STATUS_BAD_LENGTH 2   /* a seq_len outside [0, logits_width]; clamped */
+#define SILKERN_STATUS_WAIT_TIMEOUT 4 /* a bounded wait for a bulk copy gave up */
 
 /* Widest selection row either entry point accepts. */
 #define SILKERN_MAX_ROW_WIDTH 16384
@@ -185,6 +188,58 @@ int silkern_atomic_baseline_v1(const int32_t* req_ids, const int32_t* block_tabl
                                int32_t* out, int32_t* counts, int32_t* scratch, int64_t batch,
                                int64_t width, int32_t block_size, int32_t dcp_size,
                                int32_t dcp_rank, int32_t dcp_interleave, void* stream);
+
+/*
+ * Fused indexer top-k + localization: selection and conversion in one launch,
+ * without the (batch, top_k) selection round trip through HBM. This is the
+ * "fuse the converter into the indexer's top-k epilogue" step beyond the
+ * reference's converter boundary; its localization half is the contract above
+ * (silkern/contract.py:67-158), applied to the selected positions.
+ *
+ * logits is float32 (batch, logits_width) with row stride logits_stride
+ * (elements, >= logits_width); row r scores the positions [0, L) with
+ * L = seq_lens[r] (values outside [0, logits_width] are clamped and flagged
+ * with SILKERN_STATUS_BAD_LENGTH); columns at and beyond L are never read.
+ * Selection: every position when L <= top_k; otherwise the top_k positions
+ * with the largest keys, where key(x) orders the float bit patterns totally
+ * (-NaN < -inf < ... < -0 < +0 < ... < +inf < +NaN), ties going to the lower
+ * position. The selected positions, in ascending order and padded with -1 to
+ * top_k, form the selection row that is localized into out (batch, top_k)
+ * and counts (batch,), exactly as silkern_localize_rowwise_v1 would localize
+ * it. positions (batch, top_k) may be NULL; otherwise it receives that
+ * selection row. 1 <= top_k <= SILKERN_MAX_ROW_WIDTH; logits_width <=
+ * SILKERN_TOPK_MAX_WIDTH. One CTA per row: a sampled estimate of the
+ * threshold, one streaming pass over the row that keeps candidate bit masks,
+ * an exact radix select over the candidates in shared memory (or over the
+ * whole row when the estimate misses), and the converter's compaction.
+ */
+#define SILKERN_TOPK_MAX_WIDTH 262144
+int silkern_topk_localize_v1(const float* logits, int64_t logits_stride, int64_t logits_width,
+                             const int32_t* seq_lens, const int32_t* req_ids,
+                             const int32_t* block_table, int64_t table_rows, int64_t table_width,
+                             int32_t* positions, int32_t* out, int32_t* counts, int64_t batch,
+                             int32_t top_k, int32_t block_size, int32_t dcp_size, int32_t dcp_rank,
+                             int32_t dcp_interleave, int32_t compact_valid_to_front,
+                             int32_t* status, void* stream);
+
+/*
+ * silkern_topk_localize_v1 with explicit internals (tuning and test hook):
+ * candidate_capacity entries in the shared-memory candidate list (0 =
+ * automatic; top_k .. the shared-memory budget; a capacity of top_k sends
+ * almost every row down the whole-row path) and stage_table (-1 automatic,
+ * 0 gather the block table from global memory, 1 stage the request's row in
+ * shared memory, which needs table_width <= 4096). SILKERN_E_GEOMETRY when
+ * either is out of range.
+ */
+int silkern_topk_localize_explicit_v1(const float* logits, int64_t logits_stride,
+                                      int64_t logits_width, const int32_t* seq_lens,
+                                      const int32_t* req_ids, const int32_t* block_table,
+                                      int64_t table_rows, int64_t table_width, int32_t* positions,
+                                      int32_t* out, int32_t* counts, int64_t batch, int32_t top_k,
+                                      int32_t block_size, int32_t dcp_size, int32_t dcp_rank,
+                                      int32_t dcp_interleave, int32_t compact_valid_to_front,
+                                      int32_t candidate_capacity, int32_t stage_table,
+                                      int32_t* status, void* stream);
 
 /* Static text for a return code (positive SILKERN_E*, 0, or -cudaError_t). */
 const char* silkern_status_string_v1(int code);

@@ -31,6 +31,7 @@ from silkern_b200.contract import (
 )
 from silkern_b200.errors import LocalizationError
 from silkern_b200.kernels import localize_hierarchical, localize_rowwise
+from silkern_b200.topk import topk_localize
 from silkern_b200.verify import (
     CellReport,
     ConformanceReport,
@@ -58,6 +59,7 @@ __all__ = [
     "localize_hierarchical",
     "localize_reference",
     "localize_rowwise",
+    "topk_localize",
     "replay_gate",
     "workspace_shapes",
 ]

@@ -18,7 +18,11 @@ PACKAGE_DIR = os.path.dirname(os.path.abspath(__file__))
 REPO_DIR = os.path.dirname(PACKAGE_DIR)
 CSRC = os.path.join(PACKAGE_DIR, "csrc")
 INCLUDE = os.path.join(REPO_DIR, "include")
-SOURCES = [os.path.join(CSRC, "localize.cu"), os.path.join(CSRC, "atomic_baseline.cu")]
+SOURCES = [
+    os.path.join(CSRC, "localize.cu"),
+    os.path.join(CSRC, "topk_localize.cu"),
+    os.path.join(CSRC, "atomic_baseline.cu"),
+]
 DEPENDS = SOURCES + [
     os.path.join(CSRC, "fastdiv.cuh"),
     os.path.join(CSRC, "ptx.cuh"),

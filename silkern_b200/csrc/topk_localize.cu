@@ -1,0 +1,707 @@
+// Fused indexer top-k + localization on B200 (sm_100a).
+//
+// A sparse decode step scores every context position of a request (the
+// indexer's logits), keeps the top_k of them, and the converter then turns
+// those global positions into this DCP rank's physical KV slots. Run as two
+// kernels, the (batch, top_k) selection goes to HBM and comes back and the
+// second kernel pays a dependent-launch handoff. Here both are one kernel,
+// one CTA per row, every row of the batch resident at once:
+//
+//   1. estimate: a histogram of the top 11 bits of the order key over every
+//      8th float4 of the row picks a floor bin that should leave ~1.5 x top_k
+//      scores at or above it;
+//   2. stream: the row is read once from HBM (128-bit loads, several blocks
+//      in flight per warp) and only a bit mask of the candidates (scores at or
+//      above the floor) is kept, per 128-column block;
+//   3. gather: the candidates' keys and positions are collected into a list
+//      in shared memory, in position order (block offsets from a CTA scan);
+//   4. select: a three-pass radix select (11, 11 and 10 key bits) over the
+//      list finds the exact threshold key and how many keys equal to it are
+//      taken (the lowest positions);
+//   5. emit: the selected positions, in ascending order, are the selection
+//      row; the converter's contract (silkern/contract.py:67-158: ownership,
+//      deinterleave, paged translation, stable compaction, counts) is applied
+//      to it with CTA scans for the ranks, the request's block-table row
+//      staged in shared memory.
+//
+// When the estimate is off (fewer than top_k scores above the floor) or the
+// candidates overflow the list (heavy ties), the CTA finds the threshold by
+// radix passes over the whole row (served from L2) instead and lists exactly
+// the selected positions; the output is the same.
+//
+// Order key: the float's bit pattern with every bit flipped when the sign is
+// set and only the sign bit flipped otherwise, compared as unsigned. This is
+// the float order extended to a total order on bit patterns (-0 < +0, NaNs
+// outside the infinities), so the selection is deterministic for every input.
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
+
+#include "fastdiv.cuh"
+#include "ptx.cuh"
+#include "silkern_b200.h"
+
+namespace silkern {
+namespace {
+
+constexpr int kTopkThreads = 512;
+constexpr int kTopkWarps = kTopkThreads / 32;
+constexpr int kBlockCols = 128;  // one float4 per lane of a warp
+constexpr int kBins = 2048;      // 11-bit radix digit
+constexpr int kBinsPerThread = kBins / kTopkThreads;
+constexpr int kSampleEvery = 8;       // one float4 of every 8 feeds the estimate
+constexpr int kStreamUnroll = 4;      // 128-column blocks in flight per warp
+constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
+constexpr int64_t kTopkSmemBudget = 200 * 1024;  // dynamic shared memory per CTA
+constexpr int kMaxBlocks = SILKERN_TOPK_MAX_WIDTH / kBlockCols;
+constexpr int kBlocksPerThread = kMaxBlocks / kTopkThreads;
+constexpr uint32_t kAll = 0xffffffffu;
+static_assert(kBinsPerThread == 4 && kBlocksPerThread == 4, "per-thread shares of bins and blocks");
+
+struct TopkParams {
+  const float* logits;
+  const int32_t* seq_lens;
+  const int32_t* req_ids;
+  const int32_t* table;
+  int32_t* positions;  // optional selection rows
+  int32_t* out;
+  int32_t* counts;
+  int32_t* status;
+  int64_t stride;  // logits row stride (elements)
+  int64_t table_rows;
+  uint32_t table_width;
+  int32_t width;  // logits columns
+  int32_t k;
+  int32_t cap;    // candidate list capacity (entries)
+  int32_t vec;    // rows 16-byte aligned: 128-bit loads
+  int32_t stage;  // block-table row staged in shared memory
+  int32_t compact;
+  uint32_t dcp_rank, dcp_size, interleave;
+  int32_t block_size;
+  FastDiv div_il, div_dcp, div_bs;
+  // dynamic shared memory layout (byte offsets, 16-byte aligned)
+  int32_t off_boff, off_key, off_pos, off_table;
+};
+
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t bits = __float_as_uint(v);
+  return bits ^ (static_cast<uint32_t>(static_cast<int32_t>(bits) >> 31) | 0x80000000u);
+}
+
+// The float t such that !(x < t) holds for every x whose key is at least
+// `key` (and, harmlessly, for a few more: -0 when t is +0, and every NaN). A
+// key in a NaN range gives a NaN t, which admits everything.
+__device__ __forceinline__ float key_floor(uint32_t key) {
+  return __uint_as_float((key & 0x80000000u) ? (key ^ 0x80000000u) : ~key);
+}
+
+// Ownership and the logical block of position u (u >= 0): true when this
+// rank owns u and the block is inside the request's table row
+// (silkern/contract.py:132-149).
+__device__ __forceinline__ bool owned(const TopkParams& p, uint32_t u, uint32_t twidth, uint32_t* lb,
+                                      uint32_t* local) {
+  const uint32_t q1 = fastdiv(u, p.div_il);   // u / interleave
+  const uint32_t q2 = fastdiv(q1, p.div_dcp);  // u / (dcp_size * interleave)
+  *local = q2 * p.interleave + (u - q1 * p.interleave);
+  *lb = fastdiv(*local, p.div_bs);
+  return q1 - q2 * p.dcp_size == p.dcp_rank && *lb < twidth;
+}
+
+// Exclusive prefix of v over the CTA in thread order; *total gets the sum.
+// Contains two barriers; every thread of the CTA must call it.
+__device__ __forceinline__ int cta_scan(int v, int lane, int warp, int* s_scan, int* total) {
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kAll, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_scan[warp] = x;
+  __syncthreads();
+  const int w = lane < kTopkWarps ? s_scan[lane] : 0;
+  int wi = w;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kAll, wi, o);
+    if (lane >= o) wi += y;
+  }
+  const int base = __shfl_sync(kAll, wi - w, warp);
+  *total = __shfl_sync(kAll, wi, 31);
+  __syncthreads();  // s_scan may be reused
+  return base + x - v;
+}
+
+// Zero the histogram, then s_pick. s_pick is cleared after the barrier, when
+// every thread has read the previous round's pick; the caller's barrier after
+// filling the histogram orders the clear before this round's pick.
+__device__ __forceinline__ void clear_hist(uint32_t* hist, uint32_t* s_pick, int tid) {
+#pragma unroll
+  for (int b = 0; b < kBinsPerThread; ++b) hist[b * kTopkThreads + tid] = 0u;
+  __syncthreads();
+  if (tid < 4) s_pick[tid] = 0u;
+}
+
+// The histogram is complete (the caller's barrier). Finds the bin where the
+// count of keys at or above it, counted from the top, first reaches `want`:
+// s_pick = {bin, count above it, count in it, 1}; {0, 0, 0, 0} when the
+// total is below `want`. Ends with a barrier.
+__device__ __forceinline__ void pick_bin(const uint32_t* hist, uint32_t want, int tid, int lane, int warp,
+                                         int* s_scan, uint32_t* s_pick) {
+  const uint4 hv = *reinterpret_cast<const uint4*>(hist + kBinsPerThread * tid);
+  const uint32_t h[kBinsPerThread] = {hv.x, hv.y, hv.z, hv.w};
+  const uint32_t mine = h[0] + h[1] + h[2] + h[3];
+  // count in the bins of higher threads: suffix over lanes, then warps
+  uint32_t suffix = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_down_sync(kAll, suffix, o);
+    if (lane + o < 32) suffix += t;
+  }
+  if (lane == 0) s_scan[warp] = static_cast<int>(suffix);
+  __syncthreads();
+  const uint32_t wv = lane > warp && lane < kTopkWarps ? static_cast<uint32_t>(s_scan[lane]) : 0u;
+  const uint32_t above = suffix - mine + __reduce_add_sync(kAll, wv);
+  if (above < want && want <= above + mine) {
+    uint32_t a = above;
+#pragma unroll
+    for (int b = kBinsPerThread - 1; b >= 0; --b) {
+      if (a + h[b] >= want) {
+        s_pick[0] = static_cast<uint32_t>(kBinsPerThread * tid + b);
+        s_pick[1] = a;
+        s_pick[2] = h[b];
+        s_pick[3] = 1u;
+        break;
+      }
+      a += h[b];
+    }
+  }
+  __syncthreads();
+}
+
+// Scores of 128-column block b of the row (this lane's four columns); columns
+// at or past `len` read as 0 and must be masked by the caller.
+__device__ __forceinline__ float4 load_block(const float* row, int b, int lane, int len, bool vec) {
+  const int col = b * kBlockCols + 4 * lane;
+  if (vec && col + 4 <= len) return __ldg(reinterpret_cast<const float4*>(row + col));
+  float4 v;
+  v.x = col + 0 < len ? __ldg(row + col + 0) : 0.0f;
+  v.y = col + 1 < len ? __ldg(row + col + 1) : 0.0f;
+  v.z = col + 2 < len ? __ldg(row + col + 2) : 0.0f;
+  v.w = col + 3 < len ? __ldg(row + col + 3) : 0.0f;
+  return v;
+}
+
+// Rank of (lane, j) among the set bits of a block's four masks in position
+// order (lane-major, then j).
+__device__ __forceinline__ int rank_in_block(const uint32_t m[4], uint32_t lt, int lane, int j) {
+  int r = __popc(m[0] & lt) + __popc(m[1] & lt) + __popc(m[2] & lt) + __popc(m[3] & lt);
+  for (int i = 0; i < j; ++i) r += (m[i] >> lane) & 1u;
+  return r;
+}
+
+// s_boff[b] = list offset of block b (masks in s_mask, in block order), over
+// `nb` blocks, four per thread; *total gets the number of set bits.
+__device__ __forceinline__ void block_offsets(const uint4* s_mask, int32_t* s_boff, int nb, int tid, int lane,
+                                              int warp, int* s_scan, int* total) {
+  int c[kBlocksPerThread];
+  int mine = 0;
+#pragma unroll
+  for (int i = 0; i < kBlocksPerThread; ++i) {
+    const int b = kBlocksPerThread * tid + i;
+    c[i] = 0;
+    if (b < nb) {
+      const uint4 m = s_mask[b];
+      c[i] = __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+    }
+    mine += c[i];
+  }
+  int run = cta_scan(mine, lane, warp, s_scan, total);
+#pragma unroll
+  for (int i = 0; i < kBlocksPerThread; ++i) {
+    const int b = kBlocksPerThread * tid + i;
+    if (b < nb) s_boff[b] = run;
+    run += c[i];
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __grid_constant__ TopkParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint4* s_mask = reinterpret_cast<uint4*>(smem);  // per 128-column block: bit l of word j = column 4l + j
+  int32_t* s_boff = reinterpret_cast<int32_t*>(smem + p.off_boff);  // list offset per block
+  uint32_t* s_key = reinterpret_cast<uint32_t*>(smem + p.off_key);  // candidate list: order keys
+  int32_t* s_pos = reinterpret_cast<int32_t*>(smem + p.off_pos);   // ... and positions, ascending
+  int32_t* s_table = reinterpret_cast<int32_t*>(smem + p.off_table);
+  __shared__ __align__(16) uint32_t s_hist[kBins];
+  __shared__ int s_scan[kTopkWarps];
+  __shared__ uint32_t s_pick[4];
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const uint32_t lt = lanemask_lt();
+  const int64_t row = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();  // everything below may read what the previous grid wrote
+
+  int len = __ldg(p.seq_lens + row);
+  const bool bad_len = len < 0 || len > p.width;
+  len = len < 0 ? 0 : (len > p.width ? p.width : len);
+  const int32_t req = __ldg(p.req_ids + row);
+  const bool req_ok = req >= 0 && static_cast<int64_t>(req) < p.table_rows;
+  if (tid == 0 && p.status != nullptr) {
+    if (bad_len) atomicOr(p.status, SILKERN_STATUS_BAD_LENGTH);
+    if (!req_ok) atomicOr(p.status, SILKERN_STATUS_BAD_REQUEST);
+  }
+  const uint32_t twidth = req_ok ? p.table_width : 0u;
+  const int32_t* trow = p.table + static_cast<int64_t>(req_ok ? req : 0) * p.table_width;
+  if (p.stage && req_ok) {
+    for (int e = tid; e < static_cast<int>(p.table_width); e += kTopkThreads) s_table[e] = __ldg(trow + e);
+  }
+  const int k = p.k;
+  const float* lrow = p.logits + row * p.stride;
+  const bool vec = p.vec != 0;
+  const int nb = (len + kBlockCols - 1) / kBlockCols;  // blocks of the row
+
+  // The list: `total` entries in position order holding every selected
+  // position. `prefix` is the threshold key, `need` how many keys equal to it
+  // are taken, `eq_total` how many there are; `all_selected` when the list is
+  // exactly the selection (short rows, and the whole-row path).
+  int total = 0;
+  uint32_t prefix = 0;
+  int need = 0;
+  int eq_total = 0;
+  bool all_selected = true;
+
+  if (len > k) {
+    // 1. estimate from every 8th float4 (columns past len count as -NaN: they
+    // only lower the estimate)
+    clear_hist(s_hist, s_pick, tid);
+    const float pad = -__int_as_float(0x7fffffff);
+    for (int g = kSampleEvery * tid; 4 * g < len; g += kSampleEvery * kTopkThreads) {
+      const int col = 4 * g;
+      float4 v;
+      if (vec && col + 4 <= len) {
+        v = __ldg(reinterpret_cast<const float4*>(lrow + col));
+      } else {
+        v.x = __ldg(lrow + col);
+        v.y = col + 1 < len ? __ldg(lrow + col + 1) : pad;
+        v.z = col + 2 < len ? __ldg(lrow + col + 2) : pad;
+        v.w = col + 3 < len ? __ldg(lrow + col + 3) : pad;
+      }
+      atomicAdd(&s_hist[order_key(v.x) >> 21], 1u);
+      atomicAdd(&s_hist[order_key(v.y) >> 21], 1u);
+      atomicAdd(&s_hist[order_key(v.z) >> 21], 1u);
+      atomicAdd(&s_hist[order_key(v.w) >> 21], 1u);
+    }
+    __syncthreads();
+    const uint32_t want_sample = static_cast<uint32_t>(k / kSampleEvery + k / (2 * kSampleEvery) + 16);
+    pick_bin(s_hist, want_sample, tid, lane, warp, s_scan, s_pick);
+    const uint32_t lo_bin = s_pick[3] ? s_pick[0] : 0u;
+    const float floor_value = key_floor(lo_bin << 21);
+
+    // 2. stream the row once, keeping candidate masks
+    for (int b0 = warp; b0 < nb; b0 += kTopkWarps * kStreamUnroll) {
+      float4 v[kStreamUnroll];
+#pragma unroll
+      for (int u = 0; u < kStreamUnroll; ++u) {
+        const int b = b0 + u * kTopkWarps;
+        if (b < nb) v[u] = load_block(lrow, b, lane, len, vec);
+      }
+#pragma unroll
+      for (int u = 0; u < kStreamUnroll; ++u) {
+        const int b = b0 + u * kTopkWarps;
+        if (b >= nb) break;
+        const int lim = len - (b * kBlockCols + 4 * lane);
+        const uint32_t w0 = __ballot_sync(kAll, 0 < lim && !(v[u].x < floor_value));
+        const uint32_t w1 = __ballot_sync(kAll, 1 < lim && !(v[u].y < floor_value));
+        const uint32_t w2 = __ballot_sync(kAll, 2 < lim && !(v[u].z < floor_value));
+        const uint32_t w3 = __ballot_sync(kAll, 3 < lim && !(v[u].w < floor_value));
+        if (lane == 0) s_mask[b] = make_uint4(w0, w1, w2, w3);
+      }
+    }
+    __syncthreads();
+
+    // 3. list offsets per block, then gather keys and positions
+    block_offsets(s_mask, s_boff, nb, tid, lane, warp, s_scan, &total);
+    bool whole_row = total > p.cap;
+    if (!whole_row) {
+      for (int b = warp; b < nb; b += kTopkWarps) {
+        const uint4 mv = s_mask[b];
+        const uint32_t m[4] = {mv.x, mv.y, mv.z, mv.w};
+        if ((m[0] | m[1] | m[2] | m[3]) == 0u) continue;
+        int idx = s_boff[b] + rank_in_block(m, lt, lane, 0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if ((m[j] >> lane) & 1u) {
+            const int col = b * kBlockCols + 4 * lane + j;
+            s_key[idx] = order_key(__ldg(lrow + col));
+            s_pos[idx] = col;
+            ++idx;
+          }
+        }
+      }
+      __syncthreads();
+
+      // 4. exact radix select over the list
+      need = k;
+#pragma unroll 1
+      for (int pass = 0; pass < 3; ++pass) {
+        const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+        const int bits = pass == 2 ? 10 : 11;
+        clear_hist(s_hist, s_pick, tid);
+        for (int i = tid; i < total; i += kTopkThreads) {
+          const uint32_t key = s_key[i];
+          if (((key >> shift) >> bits) == prefix) atomicAdd(&s_hist[(key >> shift) & (kBins - 1)], 1u);
+        }
+        __syncthreads();
+        pick_bin(s_hist, static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
+        if (pass == 0 && !(s_pick[3] != 0u && s_pick[0] >= lo_bin)) {
+          whole_row = true;  // fewer than top_k scores above the floor
+          break;
+        }
+        prefix = (prefix << bits) | s_pick[0];
+        need -= static_cast<int>(s_pick[1]);
+        eq_total = static_cast<int>(s_pick[2]);
+      }
+      all_selected = whole_row;
+    }
+
+    if (whole_row) {
+      // Threshold from radix passes over the whole row, then list exactly the
+      // selected positions: every key above it, and the `need` lowest-
+      // positioned keys equal to it.
+      prefix = 0;
+      need = k;
+#pragma unroll 1
+      for (int pass = 0; pass < 3; ++pass) {
+        const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+        const int bits = pass == 2 ? 10 : 11;
+        clear_hist(s_hist, s_pick, tid);
+        for (int b = warp; b < nb; b += kTopkWarps) {
+          const float4 v = load_block(lrow, b, lane, len, vec);
+          const float vv[4] = {v.x, v.y, v.z, v.w};
+          const int col = b * kBlockCols + 4 * lane;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t key = order_key(vv[j]);
+            if (col + j < len && ((key >> shift) >> bits) == prefix) {
+              atomicAdd(&s_hist[(key >> shift) & (kBins - 1)], 1u);
+            }
+          }
+        }
+        __syncthreads();
+        pick_bin(s_hist, static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
+        prefix = (prefix << bits) | s_pick[0];
+        need -= static_cast<int>(s_pick[1]);
+        eq_total = static_cast<int>(s_pick[2]);
+      }
+      const bool tie_cut = eq_total != need;
+      if (tie_cut) {
+        // masks of the keys equal to the threshold, and their block offsets
+        for (int b = warp; b < nb; b += kTopkWarps) {
+          const float4 v = load_block(lrow, b, lane, len, vec);
+          const int lim = len - (b * kBlockCols + 4 * lane);
+          const uint32_t w0 = __ballot_sync(kAll, 0 < lim && order_key(v.x) == prefix);
+          const uint32_t w1 = __ballot_sync(kAll, 1 < lim && order_key(v.y) == prefix);
+          const uint32_t w2 = __ballot_sync(kAll, 2 < lim && order_key(v.z) == prefix);
+          const uint32_t w3 = __ballot_sync(kAll, 3 < lim && order_key(v.w) == prefix);
+          if (lane == 0) s_mask[b] = make_uint4(w0, w1, w2, w3);
+        }
+        __syncthreads();
+        int eqs;
+        block_offsets(s_mask, s_boff, nb, tid, lane, warp, s_scan, &eqs);
+      }
+      // selection masks (each warp rewrites only the blocks it read)
+      for (int b = warp; b < nb; b += kTopkWarps) {
+        const float4 v = load_block(lrow, b, lane, len, vec);
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+        const int lim = len - (b * kBlockCols + 4 * lane);
+        uint32_t eqm[4] = {0u, 0u, 0u, 0u};
+        int eq_base = 0;
+        if (tie_cut) {
+          const uint4 e = s_mask[b];
+          eqm[0] = e.x;
+          eqm[1] = e.y;
+          eqm[2] = e.z;
+          eqm[3] = e.w;
+          eq_base = s_boff[b];
+        }
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t key = order_key(vv[j]);
+          bool sel = j < lim && key > prefix;
+          if (j < lim && key == prefix) sel = !tie_cut || eq_base + rank_in_block(eqm, lt, lane, j) < need;
+          w[j] = __ballot_sync(kAll, sel);
+        }
+        if (lane == 0) s_mask[b] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      __syncthreads();
+      block_offsets(s_mask, s_boff, nb, tid, lane, warp, s_scan, &total);
+      total = total < p.cap ? total : p.cap;  // exactly top_k <= cap
+      for (int b = warp; b < nb; b += kTopkWarps) {
+        const uint4 mv = s_mask[b];
+        const uint32_t m[4] = {mv.x, mv.y, mv.z, mv.w};
+        if ((m[0] | m[1] | m[2] | m[3]) == 0u) continue;
+        int idx = s_boff[b] + rank_in_block(m, lt, lane, 0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if ((m[j] >> lane) & 1u) {
+            if (idx < p.cap) s_pos[idx] = b * kBlockCols + 4 * lane + j;
+            ++idx;
+          }
+        }
+      }
+    }
+  } else {
+    total = len;  // every position, listed implicitly: entry i is position i
+  }
+  __syncthreads();  // the list and the staged table row are complete
+
+  // 5. emit. Thread t owns list entries [t * per, (t + 1) * per).
+  const bool implicit = len <= k;
+  const bool rank_ties = !all_selected && eq_total != need;
+  const int per = (total + kTopkThreads - 1) / kTopkThreads;
+  const int lo = min(total, tid * per);
+  const int hi = min(total, lo + per);
+  int eq_before = 0;
+  if (rank_ties) {
+    int c = 0;
+    for (int i = lo; i < hi; ++i) c += s_key[i] == prefix ? 1 : 0;
+    int unused;
+    eq_before = cta_scan(c, lane, warp, s_scan, &unused);
+  }
+  int nsel = 0, nvalid = 0;
+  {
+    int eq_rank = eq_before;
+    for (int i = lo; i < hi; ++i) {
+      bool sel = true;
+      if (!all_selected) {
+        const uint32_t key = s_key[i];
+        sel = key > prefix;
+        if (key == prefix) sel = !rank_ties || eq_rank++ < need;
+      }
+      if (sel) {
+        ++nsel;
+        uint32_t lb, local;
+        const int32_t pos = implicit ? i : s_pos[i];
+        nvalid += owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local) ? 1 : 0;
+      }
+    }
+  }
+  // both counts in one scan: selected in the high half, valid in the low
+  int both_total;
+  const int both = cta_scan((nsel << 16) | nvalid, lane, warp, s_scan, &both_total);
+  int js = both >> 16, jv = both & 0xffff;
+  const int sel_total = both_total >> 16, valid_total = both_total & 0xffff;
+  int32_t* prow = p.positions != nullptr ? p.positions + row * k : nullptr;
+  int32_t* orow = p.out + row * k;
+  {
+    int eq_rank = eq_before;
+    for (int i = lo; i < hi; ++i) {
+      bool sel = true;
+      if (!all_selected) {
+        const uint32_t key = s_key[i];
+        sel = key > prefix;
+        if (key == prefix) sel = !rank_ties || eq_rank++ < need;
+      }
+      if (!sel) continue;
+      const int32_t pos = implicit ? i : s_pos[i];
+      uint32_t lb, local;
+      const bool valid = owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local);
+      int32_t phys = -1;
+      if (valid) {
+        const int32_t blk = p.stage ? s_table[lb] : __ldg(trow + lb);
+        phys = static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * static_cast<uint32_t>(p.block_size) + local);
+      }
+      if (prow != nullptr && js < k) prow[js] = pos;
+      if (p.compact) {
+        if (valid) {
+          if (jv < k) orow[jv] = phys;
+          ++jv;
+        }
+      } else if (js < k) {
+        orow[js] = phys;
+      }
+      ++js;
+    }
+  }
+  const int n_sel = min(sel_total, k);
+  if (prow != nullptr) {
+    for (int e = n_sel + tid; e < k; e += kTopkThreads) prow[e] = -1;
+  }
+  for (int e = (p.compact ? min(valid_total, k) : n_sel) + tid; e < k; e += kTopkThreads) orow[e] = -1;
+  if (tid == 0) p.counts[row] = valid_total;
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+bool byte_overlap(const void* a, int64_t a_bytes, const void* b, int64_t b_bytes) {
+  if (a == nullptr || b == nullptr || a_bytes <= 0 || b_bytes <= 0) return false;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + static_cast<uintptr_t>(b_bytes) && b0 < a0 + static_cast<uintptr_t>(a_bytes);
+}
+
+// Dynamic shared memory above the default needs an opt-in per kernel and
+// device; the largest size granted so far is remembered.
+int allow_topk_smem(size_t bytes) {
+  static std::mutex mutex;
+  static size_t granted[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    const cudaError_t err = cudaGetLastError();
+    return -static_cast<int>(err == cudaSuccess ? cudaErrorInvalidDevice : err);
+  }
+  std::lock_guard<std::mutex> lock(mutex);
+  if (dev >= 0 && dev < 64 && granted[dev] >= bytes) return SILKERN_OK;
+  const cudaError_t err = cudaFuncSetAttribute(topk_localize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(bytes));
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -static_cast<int>(err);
+  }
+  if (dev >= 0 && dev < 64) granted[dev] = bytes;
+  return SILKERN_OK;
+}
+
+int align16(int64_t v) { return static_cast<int>((v + 15) & ~int64_t{15}); }
+
+int topk_launch(const float* logits, int64_t stride, int64_t width, const int32_t* seq_lens,
+                const int32_t* req_ids, const int32_t* table, int64_t table_rows, int64_t table_width,
+                int32_t* positions, int32_t* out, int32_t* counts, int64_t batch, int32_t top_k,
+                int32_t block_size, int32_t dcp_size, int32_t dcp_rank, int32_t interleave, int32_t compact,
+                int32_t cap_req, int32_t stage_req, int32_t* status, cudaStream_t stream) {
+  if (!logits || !seq_lens || !req_ids || !table || !out || !counts) return SILKERN_E_NULL;
+  if (batch < 1 || batch > INT32_MAX || width < 1 || width > SILKERN_TOPK_MAX_WIDTH || stride < width ||
+      top_k < 1 || top_k > SILKERN_MAX_ROW_WIDTH || table_rows < 1 || table_width < 1 || table_width > INT32_MAX) {
+    return SILKERN_E_SHAPE;
+  }
+  if (dcp_size < 1 || dcp_rank < 0 || dcp_rank >= dcp_size || interleave < 1) return SILKERN_E_DCP;
+  if (block_size < 1 || block_size % interleave != 0) return SILKERN_E_BLOCK_SIZE;
+
+  // Inputs and outputs, in bytes, must not overlap (outputs among themselves either).
+  const int64_t logit_bytes = ((batch - 1) * stride + width) * 4;
+  struct Range {
+    const void* p;
+    int64_t bytes;
+  };
+  const Range inputs[4] = {{logits, logit_bytes}, {seq_lens, batch * 4}, {req_ids, batch * 4},
+                           {table, table_rows * table_width * 4}};
+  const Range outputs[3] = {{positions, batch * top_k * 4}, {out, batch * top_k * 4}, {counts, batch * 4}};
+  for (const Range& o : outputs) {
+    for (const Range& in : inputs) {
+      if (byte_overlap(o.p, o.bytes, in.p, in.bytes)) return SILKERN_E_ALIAS;
+    }
+  }
+  for (int a = 0; a < 3; ++a) {
+    for (int b = a + 1; b < 3; ++b) {
+      if (byte_overlap(outputs[a].p, outputs[a].bytes, outputs[b].p, outputs[b].bytes)) return SILKERN_E_ALIAS;
+    }
+  }
+
+  int stage;
+  if (stage_req < 0) {
+    stage = table_width <= kTableStageMax ? 1 : 0;
+  } else {
+    if (stage_req > 1 || (stage_req == 1 && table_width > kTableStageMax)) return SILKERN_E_GEOMETRY;
+    stage = stage_req;
+  }
+  // Candidate list: room for the usual ~1.5 x top_k candidates plus the
+  // floor bin's spill, within the shared-memory budget, never below top_k
+  // (the whole-row path lists exactly top_k). The explicit entry point may
+  // shrink it to force that path.
+  const int64_t nblocks = (width + kBlockCols - 1) / kBlockCols;
+  const int64_t fixed = align16(nblocks * 16) + align16(nblocks * 4) + (stage ? align16(table_width * 4) : 0);
+  const int64_t cap_max = (kTopkSmemBudget - fixed) / 8 / 4 * 4;
+  int64_t cap = int64_t{3} * top_k + 2048;
+  if (cap > cap_max) cap = cap_max;
+  if (cap_req != 0) {
+    if (cap_req > cap_max) return SILKERN_E_GEOMETRY;
+    cap = cap_req;
+  }
+  if (cap < top_k) return SILKERN_E_GEOMETRY;
+  TopkParams p{};
+  p.off_boff = align16(nblocks * 16);
+  p.off_key = p.off_boff + align16(nblocks * 4);
+  p.off_pos = p.off_key + align16(cap * 4);
+  p.off_table = p.off_pos + align16(cap * 4);
+  const int64_t smem = p.off_table + (stage ? align16(table_width * 4) : 0);
+  const int rc = allow_topk_smem(static_cast<size_t>(smem));
+  if (rc != SILKERN_OK) return rc;
+
+  p.logits = logits;
+  p.seq_lens = seq_lens;
+  p.req_ids = req_ids;
+  p.table = table;
+  p.positions = positions;
+  p.out = out;
+  p.counts = counts;
+  p.status = status;
+  p.stride = stride;
+  p.table_rows = table_rows;
+  p.table_width = static_cast<uint32_t>(table_width);
+  p.width = static_cast<int32_t>(width);
+  p.k = top_k;
+  p.cap = static_cast<int32_t>(cap);
+  p.vec = ((reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && stride % 4 == 0) ? 1 : 0;
+  p.stage = stage;
+  p.compact = (compact != 0 && dcp_size > 1) ? 1 : 0;
+  p.dcp_rank = static_cast<uint32_t>(dcp_rank);
+  p.dcp_size = static_cast<uint32_t>(dcp_size);
+  p.interleave = static_cast<uint32_t>(interleave);
+  p.block_size = block_size;
+  p.div_il = make_fastdiv(p.interleave);
+  p.div_dcp = make_fastdiv(p.dcp_size);
+  p.div_bs = make_fastdiv(static_cast<uint32_t>(block_size));
+
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(batch), 1, 1);
+  cfg.blockDim = dim3(kTopkThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, topk_localize_kernel, p);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -static_cast<int>(err);
+  }
+  return SILKERN_OK;
+}
+
+}  // namespace
+}  // namespace silkern
+
+extern "C" int silkern_topk_localize_v1(const float* logits, int64_t logits_stride, int64_t logits_width,
+                                        const int32_t* seq_lens, const int32_t* req_ids,
+                                        const int32_t* block_table, int64_t table_rows, int64_t table_width,
+                                        int32_t* positions, int32_t* out, int32_t* counts, int64_t batch,
+                                        int32_t top_k, int32_t block_size, int32_t dcp_size, int32_t dcp_rank,
+                                        int32_t dcp_interleave, int32_t compact_valid_to_front,
+                                        int32_t* status, void* stream) {
+  return silkern::topk_launch(logits, logits_stride, logits_width, seq_lens, req_ids, block_table, table_rows,
+                              table_width, positions, out, counts, batch, top_k, block_size, dcp_size, dcp_rank,
+                              dcp_interleave, compact_valid_to_front, 0, -1, status,
+                              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int silkern_topk_localize_explicit_v1(
+    const float* logits, int64_t logits_stride, int64_t logits_width, const int32_t* seq_lens,
+    const int32_t* req_ids, const int32_t* block_table, int64_t table_rows, int64_t table_width,
+    int32_t* positions, int32_t* out, int32_t* counts, int64_t batch, int32_t top_k, int32_t block_size,
+    int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave, int32_t compact_valid_to_front,
+    int32_t candidate_capacity, int32_t stage_table, int32_t* status, void* stream) {
+  if (candidate_capacity < 0 || stage_table < -1) return SILKERN_E_GEOMETRY;
+  return silkern::topk_launch(logits, logits_stride, logits_width, seq_lens, req_ids, block_table, table_rows,
+                              table_width, positions, out, counts, batch, top_k, block_size, dcp_size, dcp_rank,
+                              dcp_interleave, compact_valid_to_front, candidate_capacity, stage_table, status,
+                              static_cast<cudaStream_t>(stream));
+}

@@ -157,6 +157,55 @@ def test_explicit_rejects_bad_geometry(lib) -> None:
     assert call(1, chunks=1, width=16384) == 7  # 4096 granules do not fit 512 threads x 1 chunk
 
 
+LOGITS, LENS, POS = 0x100000, 0x200000, 0x300000
+
+
+def topk(lib, explicit=None, **over):
+    a = dict(logits=LOGITS, stride=4096, width=4096, lens=LENS, req=REQ, table=TABLE, rows=4, twidth=8,
+             pos=POS, out=OUT, cnt=CNT, batch=4, k=64, bs=64, dcp=2, rank=0, il=1, compact=1)
+    a.update(over)
+    args = [a["logits"], a["stride"], a["width"], a["lens"], a["req"], a["table"], a["rows"], a["twidth"],
+            a["pos"], a["out"], a["cnt"], a["batch"], a["k"], a["bs"], a["dcp"], a["rank"], a["il"],
+            a["compact"]]
+    if explicit is not None:
+        return lib.silkern_topk_localize_explicit_v1(*args, explicit[0], explicit[1], None, None)
+    return lib.silkern_topk_localize_v1(*args, None, None)
+
+
+@pytest.mark.parametrize(
+    ("override", "code"),
+    [
+        ({"logits": None}, 1),
+        ({"lens": None}, 1),
+        ({"out": None}, 1),
+        ({"batch": 0}, 2),
+        ({"width": 0}, 2),
+        ({"width": 262145, "stride": 262145}, 2),
+        ({"stride": 4095}, 2),
+        ({"k": 0}, 2),
+        ({"k": 16385}, 2),
+        ({"twidth": 0}, 2),
+        ({"dcp": 0}, 3),
+        ({"rank": 2}, 3),
+        ({"bs": 0}, 4),
+        ({"out": LOGITS + 64}, 6),  # out overlaps the logits
+        ({"pos": OUT + 4}, 6),  # positions overlap out
+        ({"cnt": LENS}, 6),
+    ],
+)
+def test_topk_rejects_before_launch(lib, override, code) -> None:
+    assert topk(lib, **override) == code
+
+
+def test_topk_explicit_rejects_bad_geometry(lib) -> None:
+    assert topk(lib, explicit=(63, -1)) == 7  # candidate list below top_k (64)
+    assert topk(lib, explicit=(1 << 20, -1)) == 7  # candidate list beyond the shared-memory budget
+    assert topk(lib, explicit=(-1, -1)) == 7
+    assert topk(lib, explicit=(0, 2)) == 7  # stage_table not -1, 0 or 1
+    assert topk(lib, explicit=(0, -2)) == 7
+    assert topk(lib, explicit=(0, 1), twidth=4097, rows=1) == 7  # too wide to stage
+
+
 def test_missing_library_fails_loudly(tmp_path) -> None:
     """No CPU or Triton fallback: without the library every launcher raises."""
     import subprocess
