@@ -1,6 +1,6 @@
 """Benchmark of the localization converter on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton|vllm|atomic]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton|vllm|fused|atomic]
                     [--config C]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
 
@@ -33,6 +33,9 @@ reference's own Triton launchers on this GPU when the reference package is
 present under baseline/_ref (a comparison arm; not part of the product).
 ``--impl vllm`` times vLLM's own non-DCP converter beside ours on the
 workload's shapes at dcp_size 1, where the two compute the same function.
+``--impl fused`` times the fused indexer top-k + localization kernel on
+256 x 65536 logits (top_k 2048, dcp 4) beside vLLM's top-k followed by the
+converter.
 """
 
 from __future__ import annotations
@@ -564,6 +567,116 @@ def run_vllm(args, rank: int, world: int) -> dict | None:
     }
 
 
+FUSED = {
+    "desc": "indexer top-k + localize: batch 256 x logits 65536 float32 (row lengths U[1024, 65536], "
+            "config 3's context lengths), top_k 2048, block_size 64, dcp_size 4, table (256,256)",
+    "batch": 256, "width": 65536, "top_k": 2048,
+}
+
+
+def _fused_sets(n_sets: int, dev):
+    """Seeded logits rows (normal scores, the row's context length per request)."""
+    import numpy as np
+    import torch
+
+    case = _case(3, seed=1000, dcp_rank=0)
+    rng = np.random.default_rng(2026)
+    lens = rng.integers(1024, FUSED["width"], size=FUSED["batch"], endpoint=True).astype(np.int32)
+    gen = torch.Generator(device=dev).manual_seed(2026)
+    sets = []
+    for _ in range(n_sets):
+        sets.append({
+            "logits": torch.randn(FUSED["batch"], FUSED["width"], device=dev, generator=gen),
+            "lens": torch.as_tensor(lens).to(dev),
+            "req": torch.as_tensor(case.req_ids).to(dev),
+            "table": torch.as_tensor(case.block_table).to(dev),
+            "out": torch.empty(FUSED["batch"], FUSED["top_k"], dtype=torch.int32, device=dev),
+            "counts": torch.empty(FUSED["batch"], dtype=torch.int32, device=dev),
+            "sel": torch.empty(FUSED["batch"], FUSED["top_k"], dtype=torch.int32, device=dev),
+        })
+    return sets, case, lens
+
+
+def run_fused(args, rank: int, world: int) -> dict | None:
+    """The fused indexer top-k + localization kernel, beside the two-kernel pipeline.
+
+    One call selects the top 2048 of every logits row and localizes the
+    selection for one DCP rank (``silkern_b200.topk_localize``). Beside it,
+    when vLLM is importable, the production pipeline it replaces: vLLM's
+    decode top-k (``torch.ops._C.persistent_topk``) then this library's
+    converter on its selection. Same rotation (4 sets of 64 MB logits, over
+    twice L2) and graph-replay timing as the other arms; the fused output of
+    one set is compared with the oracle. A comparison arm, rank 0 only.
+    """
+    if rank != 0:
+        return None
+    import numpy as np
+    import torch
+
+    from oracle.topk import topk_localize as oracle_topk
+    from silkern_b200 import localize_rowwise, topk_localize
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_sets = 4
+    sets, case, lens = _fused_sets(n_sets, dev)
+    geometry = dict(block_size=case.block_size, dcp_size=case.dcp_size, dcp_rank=0)
+
+    def fused(i):
+        d = sets[i % n_sets]
+        topk_localize(d["logits"], d["lens"], d["req"], d["table"], d["out"], d["counts"], **geometry)
+
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        fused(0)
+    torch.cuda.synchronize(dev)
+    _, want_out, want_counts = oracle_topk(sets[0]["logits"].cpu().numpy(), lens, case.req_ids, case.block_table,
+                                           top_k=FUSED["top_k"], threads=_host_threads(), **geometry)
+    bit_exact = (np.array_equal(sets[0]["out"].cpu().numpy(), want_out)
+                 and np.array_equal(sets[0]["counts"].cpu().numpy(), want_counts))
+    warm, timed = args.warmup, args.steps
+    fused_s = _replay_seconds(fused, warm, timed, stream, dev) / timed
+    pipeline_s = None
+    try:
+        import vllm._custom_ops  # noqa: F401  (registers torch.ops._C)
+
+        workspace = torch.zeros(1024 * 1024, dtype=torch.uint8, device=dev)
+        max_len = int(lens.max())
+
+        def pipeline(i):
+            d = sets[i % n_sets]
+            torch.ops._C.persistent_topk(d["logits"], d["lens"], d["sel"], workspace, FUSED["top_k"], max_len)
+            localize_rowwise(d["req"], d["table"], d["sel"], d["out"], d["counts"], **geometry)
+
+        pipeline_s = _replay_seconds(pipeline, warm, timed, stream, dev) / timed
+    except Exception:  # noqa: BLE001  (vLLM absent or its op unavailable: no comparison)
+        pipeline_s = None
+    logit_bytes = int(lens.sum()) * 4
+    out_bytes = FUSED["batch"] * FUSED["top_k"] * 4 + FUSED["batch"] * 4
+    bytes_per_call = logit_bytes + out_bytes + int(case.block_table.nbytes) + FUSED["batch"] * 8
+    peaks = _peaks()
+    achieved = bytes_per_call / fused_s / 1e9
+    return {
+        "impl": "fused-topk-localize",
+        "metric": "us per call, indexer top-k + localization (lower is better)",
+        "value": fused_s * 1e6,
+        "unit": "us/call",
+        "higher_is_better": False,
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "bit_exact": bit_exact,
+        "vllm_topk_then_converter_us": None if pipeline_s is None else pipeline_s * 1e6,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "algorithmic_bytes_per_call": bytes_per_call,
+                     "peak_source": peaks["source"]},
+        "gpu_launches": timed,
+        "config": {"workload": FUSED["desc"], "l2": f"inputs larger than L2: {n_sets} rotating logits sets"},
+        "data": "synthetic (seeded normal scores)",
+    }
+
+
 def _make_call(arm: str, bufs: dict, geometry: dict, tile_size: int):
     from silkern_b200.baselines import launch_atomic_baseline
     from silkern_b200.kernels import localize_hierarchical, localize_rowwise
@@ -836,7 +949,8 @@ def main(argv=None) -> int:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=2000)
     parser.add_argument("--warmup", type=int, default=64)
-    parser.add_argument("--impl", choices=["ours", "reference", "triton", "vllm", "atomic"], default="ours")
+    parser.add_argument("--impl", choices=["ours", "reference", "triton", "vllm", "fused", "atomic"],
+                        default="ours")
     parser.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=3)
     parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -848,9 +962,9 @@ def main(argv=None) -> int:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
-    if args.impl in ("reference", "triton", "vllm"):
-        result = {"reference": run_reference, "triton": run_triton, "vllm": run_vllm}[args.impl](
-            args, rank, world)
+    if args.impl in ("reference", "triton", "vllm", "fused"):
+        result = {"reference": run_reference, "triton": run_triton, "vllm": run_vllm,
+                  "fused": run_fused}[args.impl](args, rank, world)
         if result is not None:
             print(json.dumps(result), flush=True)
         return 0

@@ -7,15 +7,19 @@
 // second kernel pays a dependent-launch handoff. Here both are one kernel,
 // one CTA per row, every row of the batch resident at once:
 //
+//   0. as soon as the row's length is known, bulk L2 prefetches
+//      (cp.async.bulk.prefetch.L2) start the whole row streaming from HBM;
 //   1. estimate: a histogram of the top 11 bits of the order key over every
-//      8th float4 of the row picks a floor bin that should leave ~1.5 x top_k
-//      scores at or above it;
-//   2. stream: the row is read once from HBM (128-bit loads, several blocks
+//      16th float4 of the row picks a floor bin that should leave ~1.5 x
+//      top_k scores at or above it;
+//   2. stream: the row is read once (128-bit loads, several 128-column blocks
 //      in flight per warp) and only a bit mask of the candidates (scores at or
 //      above the floor) is kept, per 128-column block;
-//   3. gather: the candidates' keys and positions are collected into a list
-//      in shared memory, in position order (block offsets from a CTA scan);
-//   4. select: a three-pass radix select (11, 11 and 10 key bits) over the
+//   3. gather: a CTA scan over the blocks' candidate counts lays the
+//      candidates out in position order; their positions are written from
+//      the masks, then their keys are loaded (L2 hits) by all threads at once,
+//      feeding the first radix histogram;
+//   4. select: the three-pass radix select (11, 11 and 10 key bits) over the
 //      list finds the exact threshold key and how many keys equal to it are
 //      taken (the lowest positions);
 //   5. emit: the selected positions, in ascending order, are the selection
@@ -24,7 +28,7 @@
 //      to it with CTA scans for the ranks, the request's block-table row
 //      staged in shared memory.
 //
-// When the estimate is off (fewer than top_k scores above the floor) or the
+// When the estimate misses (fewer than top_k scores above the floor) or the
 // candidates overflow the list (heavy ties), the CTA finds the threshold by
 // radix passes over the whole row (served from L2) instead and lists exactly
 // the selected positions; the output is the same.
@@ -51,7 +55,8 @@ constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kBlockCols = 128;  // one float4 per lane of a warp
 constexpr int kBins = 2048;      // 11-bit radix digit
 constexpr int kBinsPerThread = kBins / kTopkThreads;
-constexpr int kSampleEvery = 8;       // one float4 of every 8 feeds the estimate
+constexpr int kSampleEvery = 16;      // one float4 of every 16 feeds the estimate
+constexpr int64_t kPrefetchBytes = 16384;  // per bulk L2 prefetch
 constexpr int kStreamUnroll = 4;      // 128-column blocks in flight per warp
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
 constexpr int64_t kTopkSmemBudget = 200 * 1024;  // dynamic shared memory per CTA
@@ -264,6 +269,16 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   const float* lrow = p.logits + row * p.stride;
   const bool vec = p.vec != 0;
   const int nb = (len + kBlockCols - 1) / kBlockCols;  // blocks of the row
+  if (len > k && vec) {
+    // Start the whole row streaming into L2 now; the sample and the stream
+    // pass below then mostly hit L2.
+    const int64_t bytes = static_cast<int64_t>(len & ~3) * 4;
+    for (int64_t off = static_cast<int64_t>(tid) * kPrefetchBytes; off < bytes;
+         off += static_cast<int64_t>(kTopkThreads) * kPrefetchBytes) {
+      const int64_t n = bytes - off < kPrefetchBytes ? bytes - off : kPrefetchBytes;
+      prefetch_l2_bulk(lrow + off / 4, static_cast<uint32_t>(n));
+    }
+  }
 
   // The list: `total` entries in position order holding every selected
   // position. `prefix` is the threshold key, `need` how many keys equal to it
@@ -276,8 +291,8 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   bool all_selected = true;
 
   if (len > k) {
-    // 1. estimate from every 8th float4 (columns past len count as -NaN: they
-    // only lower the estimate)
+    // 1. estimate from every 16th float4 (columns past len count as -NaN:
+    // they only lower the estimate)
     clear_hist(s_hist, s_pick, tid);
     const float pad = -__int_as_float(0x7fffffff);
     for (int g = kSampleEvery * tid; 4 * g < len; g += kSampleEvery * kTopkThreads) {
@@ -324,7 +339,9 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
     }
     __syncthreads();
 
-    // 3. list offsets per block, then gather keys and positions
+    // 3. list offsets per block; positions first (shared memory only), then
+    // the keys, loaded from L2 by all threads at once, feeding the first
+    // radix histogram
     block_offsets(s_mask, s_boff, nb, tid, lane, warp, s_scan, &total);
     bool whole_row = total > p.cap;
     if (!whole_row) {
@@ -335,28 +352,37 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         int idx = s_boff[b] + rank_in_block(m, lt, lane, 0);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          if ((m[j] >> lane) & 1u) {
-            const int col = b * kBlockCols + 4 * lane + j;
-            s_key[idx] = order_key(__ldg(lrow + col));
-            s_pos[idx] = col;
-            ++idx;
-          }
+          if ((m[j] >> lane) & 1u) s_pos[idx++] = b * kBlockCols + 4 * lane + j;
         }
+      }
+      clear_hist(s_hist, s_pick, tid);  // its barrier also publishes s_pos
+#pragma unroll 4
+      for (int i0 = warp * 32; i0 < total; i0 += kTopkThreads) {
+        const int i = i0 + lane;
+        const bool in = i < total;
+        const uint32_t key = in ? order_key(__ldg(lrow + s_pos[i])) : 0u;
+        if (in) s_key[i] = key;
+        // a warp's candidates are neighbours in the row, and their top
+        // digits cluster in few bins: one atomic per distinct bin per warp
+        const uint32_t peers = __match_any_sync(kAll, in ? key >> 21 : 0xffffffffu);
+        if (in && lane == __ffs(peers) - 1) atomicAdd(&s_hist[key >> 21], static_cast<uint32_t>(__popc(peers)));
       }
       __syncthreads();
 
-      // 4. exact radix select over the list
+      // 4. exact radix select over the list (first pass counted above)
       need = k;
 #pragma unroll 1
       for (int pass = 0; pass < 3; ++pass) {
         const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
         const int bits = pass == 2 ? 10 : 11;
-        clear_hist(s_hist, s_pick, tid);
-        for (int i = tid; i < total; i += kTopkThreads) {
-          const uint32_t key = s_key[i];
-          if (((key >> shift) >> bits) == prefix) atomicAdd(&s_hist[(key >> shift) & (kBins - 1)], 1u);
+        if (pass > 0) {
+          clear_hist(s_hist, s_pick, tid);
+          for (int i = tid; i < total; i += kTopkThreads) {
+            const uint32_t key = s_key[i];
+            if ((key >> (shift + bits)) == prefix) atomicAdd(&s_hist[(key >> shift) & (kBins - 1)], 1u);
+          }
+          __syncthreads();
         }
-        __syncthreads();
         pick_bin(s_hist, static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
         if (pass == 0 && !(s_pick[3] != 0u && s_pick[0] >= lo_bin)) {
           whole_row = true;  // fewer than top_k scores above the floor
