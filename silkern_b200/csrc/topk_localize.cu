@@ -345,14 +345,18 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
     block_offsets(s_mask, s_boff, nb, tid, lane, warp, s_scan, &total);
     bool whole_row = total > p.cap;
     if (!whole_row) {
-      for (int b = warp; b < nb; b += kTopkWarps) {
-        const uint4 mv = s_mask[b];
-        const uint32_t m[4] = {mv.x, mv.y, mv.z, mv.w};
-        if ((m[0] | m[1] | m[2] | m[3]) == 0u) continue;
-        int idx = s_boff[b] + rank_in_block(m, lt, lane, 0);
+      for (int b0 = warp; b0 < nb; b0 += kTopkWarps * kStreamUnroll) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if ((m[j] >> lane) & 1u) s_pos[idx++] = b * kBlockCols + 4 * lane + j;
+        for (int u = 0; u < kStreamUnroll; ++u) {  // independent blocks
+          const int b = b0 + u * kTopkWarps;
+          if (b >= nb) break;
+          const uint4 mv = s_mask[b];
+          const uint32_t m[4] = {mv.x, mv.y, mv.z, mv.w};
+          int idx = s_boff[b] + rank_in_block(m, lt, lane, 0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if ((m[j] >> lane) & 1u) s_pos[idx++] = b * kBlockCols + 4 * lane + j;
+          }
         }
       }
       clear_hist(s_hist, s_pick, tid);  // its barrier also publishes s_pos
@@ -361,11 +365,10 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         const int i = i0 + lane;
         const bool in = i < total;
         const uint32_t key = in ? order_key(__ldg(lrow + s_pos[i])) : 0u;
-        if (in) s_key[i] = key;
-        // a warp's candidates are neighbours in the row, and their top
-        // digits cluster in few bins: one atomic per distinct bin per warp
-        const uint32_t peers = __match_any_sync(kAll, in ? key >> 21 : 0xffffffffu);
-        if (in && lane == __ffs(peers) - 1) atomicAdd(&s_hist[key >> 21], static_cast<uint32_t>(__popc(peers)));
+        if (in) {
+          s_key[i] = key;
+          atomicAdd(&s_hist[key >> 21], 1u);
+        }
       }
       __syncthreads();
 
