@@ -52,9 +52,8 @@ extern "C" {
 #define SILKERN_E_SCRATCH 8      /* batch x tiles exceeds SILKERN_NOALLOC_MAX_TILES */
 
 #define SILKERN_STATUS_BAD_REQUEST 1
-/* Status bits of the fused top-k entry point (OR-ed into *status). */
-#define SILKERN_STATUS_BAD_LENGTH 2   /* a seq_len outside [0, logits_width]; clamped */
-#define SILKERN_STATUS_WAIT_TIMEOUT 4 /* a bounded wait for a bulk copy gave up */
+/* Status bit of the fused top-k entry point (OR-ed into *status). */
+#define SILKERN_STATUS_BAD_LENGTH 2 /* a seq_len outside [0, logits_width]; clamped */
 
 /* Widest selection row either entry point accepts. */
 #define SILKERN_MAX_ROW_WIDTH 16384

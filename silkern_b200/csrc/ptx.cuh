@@ -1,7 +1,6 @@
 // Thin inline-PTX wrappers for the sm_90+/sm_100a features the kernels use:
 // programmatic dependent launch, thread-block cluster barriers, distributed
-// shared memory, the bulk L2 prefetch, and bulk global -> shared copies
-// completed on an mbarrier.
+// shared memory stores and the bulk L2 prefetch.
 #pragma once
 
 #include <cstdint>
@@ -71,61 +70,6 @@ __device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gmem_src)
 }
 // Wait until every cp.async this thread issued has landed in shared memory.
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-// Load four consecutive 32-bit words from the copy of `local` (16-byte
-// aligned) that lives in CTA `rank` of this cluster.
-__device__ __forceinline__ uint4 ld_shared_cluster_v4(const void* local, uint32_t rank) {
-  const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(local));
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
-  uint4 v;
-  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(remote)
-               : "memory");
-  return v;
-}
-
-// mbarrier in this CTA's shared memory, expecting `count` arrivals per phase.
-__device__ __forceinline__ void mbarrier_init(uint64_t* bar, uint32_t count) {
-  const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(addr), "r"(count) : "memory");
-}
-// Make mbarrier initialisation visible to the asynchronous (bulk copy) proxy.
-__device__ __forceinline__ void fence_mbarrier_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-// Arrive once on `bar` and add `bytes` to the transaction count it waits for.
-__device__ __forceinline__ void mbarrier_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
-  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(addr), "r"(bytes)
-               : "memory");
-}
-// One probe of phase `parity` of `bar` (the hardware may suspend the thread
-// for a bounded time before answering); true once the phase has completed.
-__device__ __forceinline__ bool mbarrier_try_wait_parity(uint64_t* bar, uint32_t parity) {
-  const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(addr), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
-// from global memory of this GPU into this CTA's shared memory; completion is
-// signalled as transactions on `bar`.
-__device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
-                                              uint64_t* bar) {
-  const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
-  const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(dst), "l"(gmem_src), "r"(bytes), "r"(b)
-               : "memory");
-}
 
 __device__ __forceinline__ uint32_t lanemask_lt() {
   uint32_t m;

@@ -269,9 +269,33 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   const float* lrow = p.logits + row * p.stride;
   const bool vec = p.vec != 0;
   const int nb = (len + kBlockCols - 1) / kBlockCols;  // blocks of the row
+  // The estimate's first loads are on the critical path: issue them before
+  // anything else reaches the memory system (columns past len count as
+  // -NaN: they only lower the estimate).
+  const float pad = -__int_as_float(0x7fffffff);
+  auto sample = [&](int g) {
+    const int col = 4 * g;
+    float4 v;
+    if (vec && col + 4 <= len) {
+      v = __ldg(reinterpret_cast<const float4*>(lrow + col));
+    } else {
+      v.x = __ldg(lrow + col);
+      v.y = col + 1 < len ? __ldg(lrow + col + 1) : pad;
+      v.z = col + 2 < len ? __ldg(lrow + col + 2) : pad;
+      v.w = col + 3 < len ? __ldg(lrow + col + 3) : pad;
+    }
+    return v;
+  };
+  const int g0 = kSampleEvery * tid;
+  const int g1 = g0 + kSampleEvery * kTopkThreads;
+  float4 first[2];
+  if (len > k) {
+    if (4 * g0 < len) first[0] = sample(g0);
+    if (4 * g1 < len) first[1] = sample(g1);
+  }
   if (len > k && vec) {
-    // Start the whole row streaming into L2 now; the sample and the stream
-    // pass below then mostly hit L2.
+    // Start the whole row streaming into L2 now; the stream pass below then
+    // mostly hits L2.
     const int64_t bytes = static_cast<int64_t>(len & ~3) * 4;
     for (int64_t off = static_cast<int64_t>(tid) * kPrefetchBytes; off < bytes;
          off += static_cast<int64_t>(kTopkThreads) * kPrefetchBytes) {
@@ -291,26 +315,17 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   bool all_selected = true;
 
   if (len > k) {
-    // 1. estimate from every 16th float4 (columns past len count as -NaN:
-    // they only lower the estimate)
+    // 1. estimate from every 16th float4
     clear_hist(s_hist, s_pick, tid);
-    const float pad = -__int_as_float(0x7fffffff);
-    for (int g = kSampleEvery * tid; 4 * g < len; g += kSampleEvery * kTopkThreads) {
-      const int col = 4 * g;
-      float4 v;
-      if (vec && col + 4 <= len) {
-        v = __ldg(reinterpret_cast<const float4*>(lrow + col));
-      } else {
-        v.x = __ldg(lrow + col);
-        v.y = col + 1 < len ? __ldg(lrow + col + 1) : pad;
-        v.z = col + 2 < len ? __ldg(lrow + col + 2) : pad;
-        v.w = col + 3 < len ? __ldg(lrow + col + 3) : pad;
-      }
+    auto count = [&](const float4& v) {
       atomicAdd(&s_hist[order_key(v.x) >> 21], 1u);
       atomicAdd(&s_hist[order_key(v.y) >> 21], 1u);
       atomicAdd(&s_hist[order_key(v.z) >> 21], 1u);
       atomicAdd(&s_hist[order_key(v.w) >> 21], 1u);
-    }
+    };
+    if (4 * g0 < len) count(first[0]);
+    if (4 * g1 < len) count(first[1]);
+    for (int g = g1 + kSampleEvery * kTopkThreads; 4 * g < len; g += kSampleEvery * kTopkThreads) count(sample(g));
     __syncthreads();
     const uint32_t want_sample = static_cast<uint32_t>(k / kSampleEvery + k / (2 * kSampleEvery) + 16);
     pick_bin(s_hist, want_sample, tid, lane, warp, s_scan, s_pick);
@@ -360,8 +375,8 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         }
       }
       clear_hist(s_hist, s_pick, tid);  // its barrier also publishes s_pos
-#pragma unroll 4
-      for (int i0 = warp * 32; i0 < total; i0 += kTopkThreads) {
+#pragma unroll 8
+      for (int i0 = warp * 32; i0 < total; i0 += kTopkThreads) {  // up to 8 loads in flight per lane
         const int i = i0 + lane;
         const bool in = i < total;
         const uint32_t key = in ? order_key(__ldg(lrow + s_pos[i])) : 0u;

@@ -32,9 +32,9 @@ from silkern_b200.kernels import _check_status, _device_scope, _is_int
 
 #: Widest logits row the kernel accepts (SILKERN_TOPK_MAX_WIDTH).
 MAX_LOGITS_WIDTH = 262144
-#: Status bits (OR-ed into ``status``) besides SILKERN_STATUS_BAD_REQUEST (1).
+#: Status bit (OR-ed into ``status``) besides SILKERN_STATUS_BAD_REQUEST (1):
+#: a seq_len outside [0, logits width], clamped.
 STATUS_BAD_LENGTH = 2
-STATUS_WAIT_TIMEOUT = 4
 
 
 def topk_localize(
