@@ -103,14 +103,6 @@ __device__ __forceinline__ void fill_invalid(int32_t* row, int lo, int hi, int t
   if (tid < rest) dst[head + 4 * nvec + tid] = -1;
 }
 
-// Barrier over one row group (threads [group * n, group * n + n) of the CTA),
-// named barrier 1 + group: for a branch that is uniform over one row but not
-// over the CTA. Barriers every row group reaches stay CTA-wide
-// (__syncthreads measured faster than per-group barriers).
-__device__ __forceinline__ void group_sync(int group, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(group + 1), "r"(nthreads) : "memory");
-}
-
 // dst[0:n] = src[0:n] (src in shared memory) with 128-bit stores on the
 // aligned body of dst.
 __device__ __forceinline__ void copy_from_shared(int32_t* dst, const int32_t* src, int n, int tid,
@@ -127,18 +119,6 @@ __device__ __forceinline__ void copy_from_shared(int32_t* dst, const int32_t* sr
   }
   const int rest = n - head - 4 * nvec;
   if (tid < rest) dst[head + 4 * nvec + tid] = src[head + 4 * nvec + tid];
-}
-
-// Copy table row `src` (n entries) into shared memory with cp.async.
-__device__ __forceinline__ void stage_row_async(int32_t* dst, const int32_t* src, int n, int tid,
-                                                int nthreads) {
-  if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-    const int nvec = n >> 2;
-    for (int g = tid; g < nvec; g += nthreads) cp_async_16(dst + 4 * g, src + 4 * g);
-    for (int e = 4 * nvec + tid; e < n; e += nthreads) cp_async_4(dst + e, src + e);
-  } else {
-    for (int e = tid; e < n; e += nthreads) cp_async_4(dst + e, src + e);
-  }
 }
 
 // NC chunks of four columns per thread; CLUSTER: rows split over a cluster;
@@ -211,15 +191,6 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
 
   const int32_t req = __ldg(p.req_ids + row);
   int32_t* s_tbl = gsmem;
-  if constexpr (STAGE) {
-    // Speculate that row r belongs to request r (one selection row per
-    // request, in order) and start copying that table row into shared memory
-    // now, in parallel with the token loads; repaired below when req != r.
-    if (active && row < p.table_rows) {
-      stage_row_async(s_tbl, p.table + row * p.table_width, static_cast<int>(p.table_width), tid,
-                      nthreads);
-    }
-  }
   const bool tok_vec = (reinterpret_cast<uintptr_t>(tok) & 15u) == 0;
   int32_t val[NC][4];
 #pragma unroll
@@ -236,6 +207,16 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
       for (int j = 0; j < 4; ++j) val[i][j] = (col + j < len) ? __ldg(tok + col + j) : -1;
     }
   }
+  if constexpr (STAGE) {
+    // Speculate that row r belongs to request r (one selection row per
+    // request, in order): load that table row in the same wave as the tokens
+    // and keep it in shared memory. It is read only after the first barrier
+    // below, so its latency hides behind the tokens' and the ballots.
+    if (active && row < p.table_rows) {
+      const int32_t* srow = p.table + row * p.table_width;
+      for (int e = tid; e < static_cast<int>(p.table_width); e += nthreads) s_tbl[e] = __ldg(srow + e);
+    }
+  }
 
   const bool req_ok = req >= 0 && static_cast<int64_t>(req) < p.table_rows;
   if (!req_ok && p.status != nullptr && tid == 0) {
@@ -244,58 +225,59 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
   const int32_t* trow = p.table + static_cast<int64_t>(req_ok ? req : 0) * p.table_width;
   if constexpr (STAGE) {
     if (req_ok && static_cast<int64_t>(req) != row) {  // the same for every thread of the row group
-      // Every thread's speculative copies must land before any repair copy
-      // is issued: the two rows can differ in 16-byte alignment, and then the
-      // two passes split the entries between threads differently.
-      cp_async_wait_all();
-      group_sync(group, nthreads);
-      stage_row_async(s_tbl, trow, static_cast<int>(p.table_width), tid, nthreads);
+      // Repair: each thread overwrites exactly the entries it staged above.
+      for (int e = tid; e < static_cast<int>(p.table_width); e += nthreads) s_tbl[e] = __ldg(trow + e);
     }
-    cp_async_wait_all();
-    __syncthreads();
   }
 
-  // Map every element in place: val becomes the physical slot or -1, bits[i]
-  // marks the valid ones. A row whose request id is outside the table keeps
-  // no element (table width 0).
+  // Ownership, deinterleave and the logical block of token t; true when t is
+  // valid here. A row whose request id is outside the table keeps no element
+  // (table width 0).
   const uint32_t twidth = req_ok ? p.table_width : 0u;
+  auto map_token = [&](int32_t t, uint32_t* lb, uint32_t* local) -> bool {
+    const uint32_t u = static_cast<uint32_t>(t);
+    if constexpr (MODE == kModePow2Il1) {
+      // interleave 1: local = t >> log2(dcp), owner = t & (dcp - 1). The host
+      // checked 2^(31 - lb_shift) >= table_width, so lb < table_width also
+      // rejects negative tokens.
+      *local = u >> p.group_shift;
+      *lb = u >> p.lb_shift;
+      return *lb < twidth && (u & p.dcp_mask) == p.dcp_rank;
+    } else if constexpr (MODE == kModePow2) {
+      *local = ((u >> p.group_shift) << p.il_shift) | (u & p.il_mask);
+      *lb = *local >> p.bs_shift;
+      return t >= 0 && ((u >> p.il_shift) & p.dcp_mask) == p.dcp_rank && *lb < twidth;
+    } else {
+      const uint32_t q1 = fastdiv(u, p.div_il);   // t / interleave
+      const uint32_t q2 = fastdiv(q1, p.div_dcp);  // t / (dcp_size * interleave)
+      *local = q2 * p.interleave + (u - q1 * p.interleave);
+      *lb = fastdiv(*local, p.div_bs);
+      return t >= 0 && q1 - q2 * p.dcp_size == p.dcp_rank && *lb < twidth;  // owner == rank
+    }
+  };
+  // physical = table[lb] * block_size + (local - lb * block_size), one
+  // multiply-add, wrapping like the reference's int32 lanes.
+  auto physical = [&](int32_t blk, uint32_t lb, uint32_t local) -> int32_t {
+    return static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * p.block_size + local);
+  };
+
+  // Map every element: bits[i] marks the valid ones. Gathering from global
+  // memory, val becomes the physical slot here (or -1; compacting calls
+  // never store an invalid element); with a staged table row, val keeps the
+  // token until the table is read after the first barrier.
   uint32_t bits[NC];
 #pragma unroll
   for (int i = 0; i < NC; ++i) {
     uint32_t b = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int32_t t = val[i][j];
-      const uint32_t u = static_cast<uint32_t>(t);
-      bool ok;
       uint32_t lb, local;
-      if constexpr (MODE == kModePow2Il1) {
-        // interleave 1: local = t >> log2(dcp), owner = t & (dcp - 1). The host
-        // checked 2^(31 - lb_shift) >= table_width, so lb < table_width also
-        // rejects negative tokens.
-        local = u >> p.group_shift;
-        lb = u >> p.lb_shift;
-        ok = lb < twidth && (u & p.dcp_mask) == p.dcp_rank;
-      } else if constexpr (MODE == kModePow2) {
-        local = ((u >> p.group_shift) << p.il_shift) | (u & p.il_mask);
-        lb = local >> p.bs_shift;
-        ok = t >= 0 && ((u >> p.il_shift) & p.dcp_mask) == p.dcp_rank && lb < twidth;
-      } else {
-        const uint32_t q1 = fastdiv(u, p.div_il);   // t / interleave
-        const uint32_t q2 = fastdiv(q1, p.div_dcp);  // t / (dcp_size * interleave)
-        local = q2 * p.interleave + (u - q1 * p.interleave);
-        lb = fastdiv(local, p.div_bs);
-        ok = t >= 0 && q1 - q2 * p.dcp_size == p.dcp_rank && lb < twidth;  // owner == rank
+      const bool ok = map_token(val[i][j], &lb, &local);
+      if constexpr (!STAGE) {
+        int32_t phys = COMPACT ? 0 : -1;
+        if (ok) phys = physical(__ldg(trow + lb), lb, local);
+        val[i][j] = phys;
       }
-      // physical = table[lb] * block_size + (local - lb * block_size), one
-      // multiply-add, wrapping like the reference's int32 lanes. Compacting
-      // calls never store an invalid element, so only in-place calls need -1.
-      int32_t phys = COMPACT ? 0 : -1;
-      if (ok) {
-        const int32_t blk = STAGE ? s_tbl[lb] : __ldg(trow + lb);
-        phys = static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * p.block_size + local);
-      }
-      val[i][j] = phys;
       b |= ok ? (1u << j) : 0u;
     }
     bits[i] = b;
@@ -315,6 +297,22 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
     if (lane == 0) s_wt[i * 32 + warp] = __popc(b0) + 2 * __popc(b1) + 4 * __popc(b2);
   }
   __syncthreads();
+  if constexpr (STAGE) {
+    // the staged table row is complete: translate the valid tokens
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        int32_t phys = COMPACT ? 0 : -1;
+        if (bits[i] & (1u << j)) {
+          uint32_t lb, local;
+          (void)map_token(val[i][j], &lb, &local);
+          phys = physical(s_tbl[lb], lb, local);
+        }
+        val[i][j] = phys;
+      }
+    }
+  }
 
   // Exclusive base of (chunk i, this warp) inside the CTA: all earlier chunks,
   // then the earlier warps of chunk i.
