@@ -364,7 +364,7 @@ def _replay_seconds(launch, warm_launches: int, timed_launches: int, stream, dev
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
-        torch.cuda._sleep(200_000)  # keep the GPU busy while the replays are queued
+        torch.cuda._sleep(2_000_000)  # ~1 ms: every replay is queued before the start event
         start.record(stream)
         for g in timed:
             g.replay()
@@ -771,7 +771,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     sampler = ClockSampler(local_rank)
     with sampler:
         with torch.cuda.stream(stream):
-            torch.cuda._sleep(200_000)  # keep the GPU busy while the replays are queued
+            torch.cuda._sleep(2_000_000)  # ~1 ms: every replay is queued before the start event
             start.record(stream)
             for g in main_graphs:
                 g.replay()
