@@ -3,7 +3,10 @@
  * no Python. It allocates device buffers with the CUDA runtime, calls the
  * row-wise, hierarchical and allocation-free hierarchical entry points on the
  * same seeded batch, and checks each result against the C oracle
- * (oracle/localize_oracle.c, test infrastructure). Exit status 0 = all equal.
+ * (oracle/localize_oracle.c, test infrastructure). It then runs the fused
+ * top-k + localization entry point on distinct scores, whose selection is
+ * computed here by sorting, and localizes that selection with the oracle to
+ * check the fused output. Exit status 0 = all equal.
  */
 #include <cuda_runtime_api.h>
 #include <stdint.h>
@@ -31,6 +34,17 @@ static uint64_t lcg_state = 0x9E3779B97F4A7C15ull;
 static uint32_t lcg(void) {
   lcg_state = lcg_state * 6364136223846793005ull + 1442695040888963407ull;
   return (uint32_t)(lcg_state >> 33);
+}
+
+/* Scores of the fused check: distinct per row, the top ones spread out. */
+static const float* g_scores;
+static int by_score_desc(const void* a, const void* b) {
+  const float x = g_scores[*(const int32_t*)a], y = g_scores[*(const int32_t*)b];
+  return (x < y) - (x > y);
+}
+static int by_value(const void* a, const void* b) {
+  const int32_t x = *(const int32_t*)a, y = *(const int32_t*)b;
+  return (x > y) - (x < y);
 }
 
 static int compare(const char* what, const int32_t* got, const int32_t* want, size_t n) {
@@ -109,6 +123,59 @@ int main(void) {
                                   block_size, dcp_size, 0, interleave, 1, NULL, stream) != SILKERN_E_ALIAS) {
     fprintf(stderr, "aliased output was not rejected\n");
     ++failures;
+  }
+
+  /* fused top-k + localization: scores (batch, lw), row lengths, top k */
+  {
+    const int64_t lw = 9000;
+    const int32_t k = 700;
+    float* scores = malloc(sizeof(float) * batch * lw);
+    int32_t* lens = malloc(sizeof(int32_t) * batch);
+    int32_t* sel = malloc(sizeof(int32_t) * batch * k);
+    int32_t* order = malloc(sizeof(int32_t) * lw);
+    int32_t* fout = malloc(sizeof(int32_t) * batch * k);
+    int32_t* fwant = malloc(sizeof(int32_t) * batch * k);
+    for (int64_t r = 0; r < batch; ++r) {
+      lens[r] = (int32_t)(lcg() % (lw + 1));
+      for (int64_t c = 0; c < lw; ++c) scores[r * lw + c] = (float)((c * 7919 + r * 31) % lw) - 4000.0f;
+      g_scores = scores + r * lw;
+      for (int32_t c = 0; c < lens[r]; ++c) order[c] = c;
+      const int32_t n = lens[r] < k ? lens[r] : k;
+      if (lens[r] > k) qsort(order, (size_t)lens[r], sizeof(int32_t), by_score_desc);
+      qsort(order, (size_t)n, sizeof(int32_t), by_value); /* the selection row: ascending positions */
+      for (int32_t j = 0; j < k; ++j) sel[r * k + j] = j < n ? order[j] : -1;
+    }
+    float* d_scores;
+    int32_t *d_lens, *d_fout, *d_fcounts;
+    CHECK_CUDA(cudaMalloc((void**)&d_scores, sizeof(float) * batch * lw));
+    CHECK_CUDA(cudaMalloc((void**)&d_lens, sizeof(int32_t) * batch));
+    CHECK_CUDA(cudaMalloc((void**)&d_fout, sizeof(int32_t) * batch * k));
+    CHECK_CUDA(cudaMalloc((void**)&d_fcounts, sizeof(int32_t) * batch));
+    CHECK_CUDA(cudaMemcpy(d_scores, scores, sizeof(float) * batch * lw, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(d_lens, lens, sizeof(int32_t) * batch, cudaMemcpyHostToDevice));
+    const int32_t rank = 1;
+    if (oracle_localize(req, table, rows, twidth, sel, fwant, want_counts, batch, k, block_size, dcp_size, rank,
+                        interleave, 1, 4) != 0) {
+      fprintf(stderr, "oracle rejected the fused case\n");
+      return 3;
+    }
+    const int rc = silkern_topk_localize_v1(d_scores, lw, lw, d_lens, d_req, d_table, rows, twidth, NULL, d_fout,
+                                            d_fcounts, batch, k, block_size, dcp_size, rank, interleave, 1, NULL,
+                                            stream);
+    if (rc != SILKERN_OK) {
+      fprintf(stderr, "fused: %s\n", silkern_status_string_v1(rc));
+      return 4;
+    }
+    CHECK_CUDA(cudaMemcpyAsync(fout, d_fout, sizeof(int32_t) * batch * k, cudaMemcpyDeviceToHost, stream));
+    CHECK_CUDA(cudaMemcpyAsync(counts, d_fcounts, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, stream));
+    CHECK_CUDA(cudaStreamSynchronize(stream));
+    failures += compare("fused out", fout, fwant, (size_t)(batch * k)) +
+                compare("fused counts", counts, want_counts, (size_t)batch);
+    if (silkern_topk_localize_v1(NULL, lw, lw, d_lens, d_req, d_table, rows, twidth, NULL, d_fout, d_fcounts,
+                                 batch, k, block_size, dcp_size, rank, interleave, 1, NULL, stream) != SILKERN_E_NULL) {
+      fprintf(stderr, "NULL logits were not rejected\n");
+      ++failures;
+    }
   }
   printf("%s (abi %d)\n", failures ? "FAILED" : "ok", silkern_abi_version_v1());
   return failures ? 1 : 0;

@@ -2,7 +2,8 @@
 
 CPU: the header compiles as C11 and the program links against the library.
 GPU: the program runs all three localization entry points and compares them
-with the C oracle.
+with the C oracle, then runs the fused top-k entry point on distinct scores
+and checks it against a selection sorted in C, localized by the oracle.
 """
 
 from __future__ import annotations
