@@ -228,7 +228,7 @@ def _oracle_step(cases, threads: int) -> None:
         oracle.localize(case.req_ids, case.block_table, case.tokens, threads=threads, **case.geometry())
 
 
-def _cpu_baseline(config: int, threads: int, seconds: float = 2.0) -> dict:
+def _cpu_baseline(config: int, threads: int, seconds: float = 10.0) -> dict:
     """The C oracle (restatement of the reference's localize_reference) on host cores."""
     calls = WORKLOADS[config]["calls"]
     cases = [_case(config, seed=layer, dcp_rank=0) for layer in range(calls)]
