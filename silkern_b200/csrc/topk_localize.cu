@@ -518,6 +518,8 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
     int unused;
     eq_before = cta_scan(c, lane, warp, s_scan, &unused);
   }
+  // Count pass; each entry's key slot (this thread's own entries, keys no
+  // longer needed) then holds its flags: bit 0 selected, bit 1 valid.
   int nsel = 0, nvalid = 0;
   {
     int eq_rank = eq_before;
@@ -528,12 +530,16 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         sel = key > prefix;
         if (key == prefix) sel = !rank_ties || eq_rank++ < need;
       }
+      uint32_t flags = 0u;
       if (sel) {
         ++nsel;
         uint32_t lb, local;
         const int32_t pos = implicit ? i : s_pos[i];
-        nvalid += owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local) ? 1 : 0;
+        const bool valid = owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local);
+        nvalid += valid ? 1 : 0;
+        flags = valid ? 3u : 1u;
       }
+      s_key[i] = flags;
     }
   }
   // both counts in one scan: selected in the high half, valid in the low
@@ -543,35 +549,28 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   const int sel_total = both_total >> 16, valid_total = both_total & 0xffff;
   int32_t* prow = p.positions != nullptr ? p.positions + row * k : nullptr;
   int32_t* orow = p.out + row * k;
-  {
-    int eq_rank = eq_before;
-    for (int i = lo; i < hi; ++i) {
-      bool sel = true;
-      if (!all_selected) {
-        const uint32_t key = s_key[i];
-        sel = key > prefix;
-        if (key == prefix) sel = !rank_ties || eq_rank++ < need;
-      }
-      if (!sel) continue;
-      const int32_t pos = implicit ? i : s_pos[i];
+  for (int i = lo; i < hi; ++i) {
+    const uint32_t flags = s_key[i];
+    if (!(flags & 1u)) continue;
+    const int32_t pos = implicit ? i : s_pos[i];
+    const bool valid = (flags & 2u) != 0u;
+    int32_t phys = -1;
+    if (valid) {
       uint32_t lb, local;
-      const bool valid = owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local);
-      int32_t phys = -1;
-      if (valid) {
-        const int32_t blk = p.stage ? s_table[lb] : __ldg(trow + lb);
-        phys = static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * static_cast<uint32_t>(p.block_size) + local);
-      }
-      if (prow != nullptr && js < k) prow[js] = pos;
-      if (p.compact) {
-        if (valid) {
-          if (jv < k) orow[jv] = phys;
-          ++jv;
-        }
-      } else if (js < k) {
-        orow[js] = phys;
-      }
-      ++js;
+      (void)owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local);
+      const int32_t blk = p.stage ? s_table[lb] : __ldg(trow + lb);
+      phys = static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * static_cast<uint32_t>(p.block_size) + local);
     }
+    if (prow != nullptr && js < k) prow[js] = pos;
+    if (p.compact) {
+      if (valid) {
+        if (jv < k) orow[jv] = phys;
+        ++jv;
+      }
+    } else if (js < k) {
+      orow[js] = phys;
+    }
+    ++js;
   }
   const int n_sel = min(sel_total, k);
   if (prow != nullptr) {
