@@ -22,9 +22,11 @@
 //      gives each warp its base; across a cluster, each CTA pushes its total
 //      into every CTA's shared memory (DSMEM) before one cluster barrier.
 //      No atomics, so the order is the selector's order on every run;
-//   4. each survivor is stored at its final position (a warp's survivors are
-//      one contiguous run), the -1 tail with 128-bit stores; every output
-//      element is written exactly once.
+//   4. survivors are staged in shared memory at their final positions, then
+//      each thread writes its output granules once with 128-bit stores
+//      (survivors, then -1); across a cluster, a CTA's survivors are one
+//      contiguous run, copied out 128-bit wide, plus the -1 tail of its own
+//      slice. Every output element is written exactly once.
 //
 // Semantics follow silkern/contract.py:67-158 (localize_reference) and the
 // int32 lanes of silkern/kernels.py:51-125 (_rowwise_kernel).
