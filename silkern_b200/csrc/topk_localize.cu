@@ -138,21 +138,18 @@ __device__ __forceinline__ int cta_scan(int v, int lane, int warp, int* s_scan, 
   return base + x - v;
 }
 
-// Zero the histogram, then s_pick. s_pick is cleared after the barrier, when
-// every thread has read the previous round's pick; the caller's barrier after
-// filling the histogram orders the clear before this round's pick.
-__device__ __forceinline__ void clear_hist(uint32_t* hist, uint32_t* s_pick, int tid) {
+// Zero a histogram; a later barrier orders it before the next fill.
+__device__ __forceinline__ void zero_hist(uint32_t* hist, int tid) {
 #pragma unroll
   for (int b = 0; b < kBinsPerThread; ++b) hist[b * kTopkThreads + tid] = 0u;
-  __syncthreads();
-  if (tid < 4) s_pick[tid] = 0u;
 }
 
-// The histogram is complete (the caller's barrier). Finds the bin where the
-// count of keys at or above it, counted from the top, first reaches `want`:
-// s_pick = {bin, count above it, count in it, 1}; {0, 0, 0, 0} when the
-// total is below `want`. Ends with a barrier.
-__device__ __forceinline__ void pick_bin(const uint32_t* hist, uint32_t want, int tid, int lane, int warp,
+// The histogram is complete (the caller's barrier). Returns whether its total
+// reaches `want`; if so, the bin where the count of keys at or above it,
+// counted from the top, first reaches `want` is published as s_pick = {bin,
+// count above it, count in it}. Ends with a barrier. (s_pick is written only
+// after the first barrier here, when every thread has read the last pick.)
+__device__ __forceinline__ bool pick_bin(const uint32_t* hist, uint32_t want, int tid, int lane, int warp,
                                          int* s_scan, uint32_t* s_pick) {
   const uint4 hv = *reinterpret_cast<const uint4*>(hist + kBinsPerThread * tid);
   const uint32_t h[kBinsPerThread] = {hv.x, hv.y, hv.z, hv.w};
@@ -166,8 +163,9 @@ __device__ __forceinline__ void pick_bin(const uint32_t* hist, uint32_t want, in
   }
   if (lane == 0) s_scan[warp] = static_cast<int>(suffix);
   __syncthreads();
-  const uint32_t wv = lane > warp && lane < kTopkWarps ? static_cast<uint32_t>(s_scan[lane]) : 0u;
-  const uint32_t above = suffix - mine + __reduce_add_sync(kAll, wv);
+  const uint32_t wt = lane < kTopkWarps ? static_cast<uint32_t>(s_scan[lane]) : 0u;
+  const uint32_t above = suffix - mine + __reduce_add_sync(kAll, lane > warp ? wt : 0u);
+  const uint32_t all = __reduce_add_sync(kAll, wt);
   if (above < want && want <= above + mine) {
     uint32_t a = above;
 #pragma unroll
@@ -176,13 +174,13 @@ __device__ __forceinline__ void pick_bin(const uint32_t* hist, uint32_t want, in
         s_pick[0] = static_cast<uint32_t>(kBinsPerThread * tid + b);
         s_pick[1] = a;
         s_pick[2] = h[b];
-        s_pick[3] = 1u;
         break;
       }
       a += h[b];
     }
   }
   __syncthreads();
+  return all >= want;
 }
 
 // Scores of 128-column block b of the row (this lane's four columns); columns
@@ -239,9 +237,9 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   uint32_t* s_key = reinterpret_cast<uint32_t*>(smem + p.off_key);  // candidate list: order keys
   int32_t* s_pos = reinterpret_cast<int32_t*>(smem + p.off_pos);   // ... and positions, ascending
   int32_t* s_table = reinterpret_cast<int32_t*>(smem + p.off_table);
-  __shared__ __align__(16) uint32_t s_hist[kBins];
+  __shared__ __align__(16) uint32_t s_hist[2][kBins];  // alternate between radix passes
   __shared__ int s_scan[kTopkWarps];
-  __shared__ uint32_t s_pick[4];
+  __shared__ uint32_t s_pick[3];
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -316,21 +314,23 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
 
   if (len > k) {
     // 1. estimate from every 16th float4
-    clear_hist(s_hist, s_pick, tid);
+    zero_hist(s_hist[0], tid);
+    zero_hist(s_hist[1], tid);
+    __syncthreads();
     auto count = [&](const float4& v) {
-      atomicAdd(&s_hist[order_key(v.x) >> 21], 1u);
-      atomicAdd(&s_hist[order_key(v.y) >> 21], 1u);
-      atomicAdd(&s_hist[order_key(v.z) >> 21], 1u);
-      atomicAdd(&s_hist[order_key(v.w) >> 21], 1u);
+      atomicAdd(&s_hist[0][order_key(v.x) >> 21], 1u);
+      atomicAdd(&s_hist[0][order_key(v.y) >> 21], 1u);
+      atomicAdd(&s_hist[0][order_key(v.z) >> 21], 1u);
+      atomicAdd(&s_hist[0][order_key(v.w) >> 21], 1u);
     };
     if (4 * g0 < len) count(first[0]);
     if (4 * g1 < len) count(first[1]);
     for (int g = g1 + kSampleEvery * kTopkThreads; 4 * g < len; g += kSampleEvery * kTopkThreads) count(sample(g));
     __syncthreads();
     const uint32_t want_sample = static_cast<uint32_t>(k / kSampleEvery + k / (2 * kSampleEvery) + 16);
-    pick_bin(s_hist, want_sample, tid, lane, warp, s_scan, s_pick);
-    const uint32_t lo_bin = s_pick[3] ? s_pick[0] : 0u;
+    const uint32_t lo_bin = pick_bin(s_hist[0], want_sample, tid, lane, warp, s_scan, s_pick) ? s_pick[0] : 0u;
     const float floor_value = key_floor(lo_bin << 21);
+    zero_hist(s_hist[0], tid);  // the first radix pass's (the barriers below order it)
 
     // 2. stream the row once, keeping candidate masks
     for (int b0 = warp; b0 < nb; b0 += kTopkWarps * kStreamUnroll) {
@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
           }
         }
       }
-      clear_hist(s_hist, s_pick, tid);  // its barrier also publishes s_pos
+      __syncthreads();  // publishes s_pos
 #pragma unroll 8
       for (int i0 = warp * 32; i0 < total; i0 += kTopkThreads) {  // up to 8 loads in flight per lane
         const int i = i0 + lane;
@@ -382,27 +382,29 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         const uint32_t key = in ? order_key(__ldg(lrow + s_pos[i])) : 0u;
         if (in) {
           s_key[i] = key;
-          atomicAdd(&s_hist[key >> 21], 1u);
+          atomicAdd(&s_hist[0][key >> 21], 1u);
         }
       }
       __syncthreads();
 
-      // 4. exact radix select over the list (first pass counted above)
+      // 4. exact radix select over the list (first pass counted above). The
+      // passes alternate histograms: each pass clears the one the next uses.
       need = k;
 #pragma unroll 1
       for (int pass = 0; pass < 3; ++pass) {
         const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
         const int bits = pass == 2 ? 10 : 11;
+        uint32_t* hist = s_hist[pass & 1];
         if (pass > 0) {
-          clear_hist(s_hist, s_pick, tid);
+          if (pass == 1) zero_hist(s_hist[0], tid);
           for (int i = tid; i < total; i += kTopkThreads) {
             const uint32_t key = s_key[i];
-            if ((key >> (shift + bits)) == prefix) atomicAdd(&s_hist[(key >> shift) & (kBins - 1)], 1u);
+            if ((key >> (shift + bits)) == prefix) atomicAdd(&hist[(key >> shift) & (kBins - 1)], 1u);
           }
           __syncthreads();
         }
-        pick_bin(s_hist, static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
-        if (pass == 0 && !(s_pick[3] != 0u && s_pick[0] >= lo_bin)) {
+        const bool found = pick_bin(hist, static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
+        if (pass == 0 && !(found && s_pick[0] >= lo_bin)) {
           whole_row = true;  // fewer than top_k scores above the floor
           break;
         }
@@ -423,7 +425,8 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
       for (int pass = 0; pass < 3; ++pass) {
         const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
         const int bits = pass == 2 ? 10 : 11;
-        clear_hist(s_hist, s_pick, tid);
+        zero_hist(s_hist[0], tid);
+        __syncthreads();
         for (int b = warp; b < nb; b += kTopkWarps) {
           const float4 v = load_block(lrow, b, lane, len, vec);
           const float vv[4] = {v.x, v.y, v.z, v.w};
@@ -432,12 +435,12 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
           for (int j = 0; j < 4; ++j) {
             const uint32_t key = order_key(vv[j]);
             if (col + j < len && ((key >> shift) >> bits) == prefix) {
-              atomicAdd(&s_hist[(key >> shift) & (kBins - 1)], 1u);
+              atomicAdd(&s_hist[0][(key >> shift) & (kBins - 1)], 1u);
             }
           }
         }
         __syncthreads();
-        pick_bin(s_hist, static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
+        (void)pick_bin(s_hist[0], static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
         prefix = (prefix << bits) | s_pick[0];
         need -= static_cast<int>(s_pick[1]);
         eq_total = static_cast<int>(s_pick[2]);
