@@ -736,13 +736,36 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
 }
 
 // Dynamic shared memory above 48 KB must be enabled per kernel and device.
+// The largest size granted so far is remembered per kernel and device, so a
+// steady stream of calls makes the driver call once.
 int allow_large_smem(KernelFn fn, size_t bytes) {
+  struct Grant {
+    KernelFn fn;
+    int device;
+    size_t bytes;
+  };
+  static std::mutex mutex;
+  static Grant grants[256];
+  static int n_grants = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    const cudaError_t err = cudaGetLastError();
+    return -static_cast<int>(err == cudaSuccess ? cudaErrorInvalidDevice : err);
+  }
+  std::lock_guard<std::mutex> lock(mutex);
+  Grant* slot = nullptr;
+  for (int i = 0; i < n_grants; ++i) {
+    if (grants[i].fn == fn && grants[i].device == dev) slot = &grants[i];
+  }
+  if (slot != nullptr && slot->bytes >= bytes) return SILKERN_OK;
   const cudaError_t err =
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
   if (err != cudaSuccess) {
     (void)cudaGetLastError();
     return -static_cast<int>(err);
   }
+  if (slot == nullptr && n_grants < 256) slot = &grants[n_grants++];
+  if (slot != nullptr) *slot = Grant{fn, dev, bytes};
   return SILKERN_OK;
 }
 
