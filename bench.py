@@ -574,27 +574,28 @@ FUSED = {
 }
 
 
-def _fused_sets(n_sets: int, dev):
+def _fused_sets(n_sets: int, batch: int, dev):
     """Seeded logits rows (normal scores, the row's context length per request)."""
     import numpy as np
     import torch
 
     case = _case(3, seed=1000, dcp_rank=0)
     rng = np.random.default_rng(2026)
-    lens = rng.integers(1024, FUSED["width"], size=FUSED["batch"], endpoint=True).astype(np.int32)
+    lens = rng.integers(1024, FUSED["width"], size=batch, endpoint=True).astype(np.int32)
+    req = np.resize(case.req_ids, batch).astype(np.int32)  # the workload's requests, repeated
     gen = torch.Generator(device=dev).manual_seed(2026)
     sets = []
     for _ in range(n_sets):
         sets.append({
-            "logits": torch.randn(FUSED["batch"], FUSED["width"], device=dev, generator=gen),
+            "logits": torch.randn(batch, FUSED["width"], device=dev, generator=gen),
             "lens": torch.as_tensor(lens).to(dev),
-            "req": torch.as_tensor(case.req_ids).to(dev),
+            "req": torch.as_tensor(req).to(dev),
             "table": torch.as_tensor(case.block_table).to(dev),
-            "out": torch.empty(FUSED["batch"], FUSED["top_k"], dtype=torch.int32, device=dev),
-            "counts": torch.empty(FUSED["batch"], dtype=torch.int32, device=dev),
-            "sel": torch.empty(FUSED["batch"], FUSED["top_k"], dtype=torch.int32, device=dev),
+            "out": torch.empty(batch, FUSED["top_k"], dtype=torch.int32, device=dev),
+            "counts": torch.empty(batch, dtype=torch.int32, device=dev),
+            "sel": torch.empty(batch, FUSED["top_k"], dtype=torch.int32, device=dev),
         })
-    return sets, case, lens
+    return sets, case, lens, req
 
 
 def run_fused(args, rank: int, world: int) -> dict | None:
@@ -604,9 +605,11 @@ def run_fused(args, rank: int, world: int) -> dict | None:
     selection for one DCP rank (``silkern_b200.topk_localize``). Beside it,
     when vLLM is importable, the production pipeline it replaces: vLLM's
     decode top-k (``torch.ops._C.persistent_topk``) then this library's
-    converter on its selection. Same rotation (4 sets of 64 MB logits, over
-    twice L2) and graph-replay timing as the other arms; the fused output of
-    one set is compared with the oracle. A comparison arm, rank 0 only.
+    converter on its selection. Same graph-replay timing as the other arms,
+    with the logits rotating over at least 4 sets and 256 MB (twice L2; 4 sets
+    of 64 MB at the default 256 rows, ``--batch`` sets the rows); the fused
+    output of one set is compared with the oracle. A comparison arm, rank 0
+    only.
     """
     if rank != 0:
         return None
@@ -618,8 +621,10 @@ def run_fused(args, rank: int, world: int) -> dict | None:
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    n_sets = 4
-    sets, case, lens = _fused_sets(n_sets, dev)
+    batch = args.batch if args.batch > 0 else FUSED["batch"]
+    # at least 4 sets and about 256 MB of logits rotating (over twice L2)
+    n_sets = max(4, -(-1024 // batch))
+    sets, case, lens, req = _fused_sets(n_sets, batch, dev)
     geometry = dict(block_size=case.block_size, dcp_size=case.dcp_size, dcp_rank=0)
 
     def fused(i):
@@ -631,7 +636,7 @@ def run_fused(args, rank: int, world: int) -> dict | None:
     with torch.cuda.stream(stream):
         fused(0)
     torch.cuda.synchronize(dev)
-    _, want_out, want_counts = oracle_topk(sets[0]["logits"].cpu().numpy(), lens, case.req_ids, case.block_table,
+    _, want_out, want_counts = oracle_topk(sets[0]["logits"].cpu().numpy(), lens, req, case.block_table,
                                            top_k=FUSED["top_k"], threads=_host_threads(), **geometry)
     bit_exact = (np.array_equal(sets[0]["out"].cpu().numpy(), want_out)
                  and np.array_equal(sets[0]["counts"].cpu().numpy(), want_counts))
@@ -653,8 +658,8 @@ def run_fused(args, rank: int, world: int) -> dict | None:
     except Exception:  # noqa: BLE001  (vLLM absent or its op unavailable: no comparison)
         pipeline_s = None
     logit_bytes = int(lens.sum()) * 4
-    out_bytes = FUSED["batch"] * FUSED["top_k"] * 4 + FUSED["batch"] * 4
-    bytes_per_call = logit_bytes + out_bytes + int(case.block_table.nbytes) + FUSED["batch"] * 8
+    out_bytes = batch * FUSED["top_k"] * 4 + batch * 4
+    bytes_per_call = logit_bytes + out_bytes + int(case.block_table.nbytes) + batch * 8
     peaks = _peaks()
     achieved = bytes_per_call / fused_s / 1e9
     return {
@@ -672,7 +677,9 @@ def run_fused(args, rank: int, world: int) -> dict | None:
                      "frac": achieved / peaks["hbm_gbs"], "algorithmic_bytes_per_call": bytes_per_call,
                      "peak_source": peaks["source"]},
         "gpu_launches": timed,
-        "config": {"workload": FUSED["desc"], "l2": f"inputs larger than L2: {n_sets} rotating logits sets"},
+        "config": {"workload": FUSED["desc"] if batch == FUSED["batch"] else
+                   FUSED["desc"].replace("batch 256", f"batch {batch}"),
+                   "batch": batch, "l2": f"inputs larger than L2: {n_sets} rotating logits sets"},
         "data": "synthetic (seeded normal scores)",
     }
 
@@ -980,6 +987,7 @@ def main(argv=None) -> int:
     parser.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=3)
     parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--batch", type=int, default=0, help="rows of the fused arm (default 256)")
     args = parser.parse_args(argv)
     if args.steps < 1 or args.warmup < 0:
         parser.error("--steps must be >= 1 and --warmup >= 0")
