@@ -15,18 +15,19 @@
 //   2. stream: the row is read once (128-bit loads, several 128-column blocks
 //      in flight per warp) and only a bit mask of the candidates (scores at or
 //      above the floor) is kept, per 128-column block;
-//   3. gather: a CTA scan over the blocks' candidate counts lays the
-//      candidates out in position order; their positions are written from
-//      the masks, then their keys are loaded (L2 hits) by all threads at once,
-//      feeding the first radix histogram;
+//   3. gather: every thread owns a run of whole blocks; one CTA scan over
+//      the threads' candidate counts gives each its offset in the list, and it
+//      writes its candidates' positions from the masks, then loads their keys
+//      (L2 hits, eight in flight), feeding the first radix histogram;
 //   4. select: the three-pass radix select (11, 11 and 10 key bits) over the
 //      list finds the exact threshold key and how many keys equal to it are
 //      taken (the lowest positions);
 //   5. emit: the selected positions, in ascending order, are the selection
 //      row; the converter's contract (silkern/contract.py:67-158: ownership,
 //      deinterleave, paged translation, stable compaction, counts) is applied
-//      to it with CTA scans for the ranks, the request's block-table row
-//      staged in shared memory.
+//      to it. Warps take contiguous runs of the list, lanes consecutive
+//      entries; ranks come from ballots and one exchange of the warps' totals,
+//      and the request's block-table row is staged in shared memory.
 //
 // When the estimate misses (fewer than top_k scores above the floor) or the
 // candidates overflow the list (heavy ties), the CTA finds the threshold by
@@ -57,7 +58,7 @@ constexpr int kBins = 2048;      // 11-bit radix digit
 constexpr int kBinsPerThread = kBins / kTopkThreads;
 constexpr int kSampleEvery = 16;      // one float4 of every 16 feeds the estimate
 constexpr int64_t kPrefetchBytes = 16384;  // per bulk L2 prefetch
-constexpr int kStreamUnroll = 4;      // 128-column blocks in flight per warp
+constexpr int kStreamUnroll = 8;      // 128-column blocks in flight per warp
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
 constexpr int64_t kTopkSmemBudget = 200 * 1024;  // dynamic shared memory per CTA
 constexpr int kMaxBlocks = SILKERN_TOPK_MAX_WIDTH / kBlockCols;
@@ -230,6 +231,45 @@ __device__ __forceinline__ void block_offsets(const uint4* s_mask, int32_t* s_bo
   __syncthreads();
 }
 
+// Lays the set bits of the blocks' masks (s_mask, `nb` blocks) out in
+// position order: thread t owns a contiguous run of whole blocks, one CTA scan
+// gives its first list index, and it writes the positions of its own set bits
+// (those below `cap`). Returns that first index; *mine gets the thread's count
+// and *total the CTA's. Contains the scan's barriers; every thread must call it.
+__device__ __forceinline__ int list_positions(const uint4* s_mask, int nb, int tid, int lane, int warp,
+                                              int* s_scan, int32_t* s_pos, int cap, int* mine, int* total) {
+  const int per = (nb + kTopkThreads - 1) / kTopkThreads;
+  const int b_lo = min(nb, tid * per);
+  const int b_hi = min(nb, b_lo + per);
+  int c = 0;
+  for (int b = b_lo; b < b_hi; ++b) {
+    const uint4 m = s_mask[b];
+    c += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
+  }
+  const int first = cta_scan(c, lane, warp, s_scan, total);
+  int idx = first;
+  for (int b = b_lo; b < b_hi; ++b) {
+    const uint4 m = s_mask[b];
+    uint32_t any = m.x | m.y | m.z | m.w;
+    const int base = b * kBlockCols;
+    while (any != 0u) {  // lanes of the block in order; a lane's four columns in order
+      const int l = __ffs(any) - 1;
+      any &= any - 1u;
+      const int col = base + 4 * l;
+      if (((m.x >> l) & 1u) && idx < cap) s_pos[idx] = col;
+      idx += (m.x >> l) & 1u;
+      if (((m.y >> l) & 1u) && idx < cap) s_pos[idx] = col + 1;
+      idx += (m.y >> l) & 1u;
+      if (((m.z >> l) & 1u) && idx < cap) s_pos[idx] = col + 2;
+      idx += (m.z >> l) & 1u;
+      if (((m.w >> l) & 1u) && idx < cap) s_pos[idx] = col + 3;
+      idx += (m.w >> l) & 1u;
+    }
+  }
+  *mine = c;
+  return first;
+}
+
 __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __grid_constant__ TopkParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   uint4* s_mask = reinterpret_cast<uint4*>(smem);  // per 128-column block: bit l of word j = column 4l + j
@@ -354,35 +394,25 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
     }
     __syncthreads();
 
-    // 3. list offsets per block; positions first (shared memory only), then
-    // the keys, loaded from L2 by all threads at once, feeding the first
-    // radix histogram
-    block_offsets(s_mask, s_boff, nb, tid, lane, warp, s_scan, &total);
+    // 3. the list in position order: each thread lists the candidates of its
+    // own blocks, then loads their keys (L2 hits, eight in flight), which
+    // feed the first radix histogram
+    int mine;
+    const int first = list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &mine, &total);
     bool whole_row = total > p.cap;
     if (!whole_row) {
-      for (int b0 = warp; b0 < nb; b0 += kTopkWarps * kStreamUnroll) {
+      for (int i0 = first; i0 < first + mine; i0 += 8) {
+        uint32_t kk[8];
 #pragma unroll
-        for (int u = 0; u < kStreamUnroll; ++u) {  // independent blocks
-          const int b = b0 + u * kTopkWarps;
-          if (b >= nb) break;
-          const uint4 mv = s_mask[b];
-          const uint32_t m[4] = {mv.x, mv.y, mv.z, mv.w};
-          int idx = s_boff[b] + rank_in_block(m, lt, lane, 0);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if ((m[j] >> lane) & 1u) s_pos[idx++] = b * kBlockCols + 4 * lane + j;
-          }
+        for (int u = 0; u < 8; ++u) {
+          kk[u] = i0 + u < first + mine ? order_key(__ldg(lrow + s_pos[i0 + u])) : 0u;
         }
-      }
-      __syncthreads();  // publishes s_pos
-#pragma unroll 8
-      for (int i0 = warp * 32; i0 < total; i0 += kTopkThreads) {  // up to 8 loads in flight per lane
-        const int i = i0 + lane;
-        const bool in = i < total;
-        const uint32_t key = in ? order_key(__ldg(lrow + s_pos[i])) : 0u;
-        if (in) {
-          s_key[i] = key;
-          atomicAdd(&s_hist[0][key >> 21], 1u);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (i0 + u < first + mine) {
+            s_key[i0 + u] = kk[u];
+            atomicAdd(&s_hist[0][kk[u] >> 21], 1u);
+          }
         }
       }
       __syncthreads();
@@ -487,93 +517,105 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         if (lane == 0) s_mask[b] = make_uint4(w[0], w[1], w[2], w[3]);
       }
       __syncthreads();
-      block_offsets(s_mask, s_boff, nb, tid, lane, warp, s_scan, &total);
+      int unused;
+      (void)list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &unused, &total);
       total = total < p.cap ? total : p.cap;  // exactly top_k <= cap
-      for (int b = warp; b < nb; b += kTopkWarps) {
-        const uint4 mv = s_mask[b];
-        const uint32_t m[4] = {mv.x, mv.y, mv.z, mv.w};
-        if ((m[0] | m[1] | m[2] | m[3]) == 0u) continue;
-        int idx = s_boff[b] + rank_in_block(m, lt, lane, 0);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if ((m[j] >> lane) & 1u) {
-            if (idx < p.cap) s_pos[idx] = b * kBlockCols + 4 * lane + j;
-            ++idx;
-          }
-        }
-      }
     }
   } else {
     total = len;  // every position, listed implicitly: entry i is position i
   }
   __syncthreads();  // the list and the staged table row are complete
 
-  // 5. emit. Thread t owns list entries [t * per, (t + 1) * per).
+  // 5. emit. Warp w owns list entries [w * seg, (w + 1) * seg), seg a
+  // multiple of 32, its lanes on consecutive entries; ranks come from
+  // ballots and one exchange of the warps' totals.
   const bool implicit = len <= k;
   const bool rank_ties = !all_selected && eq_total != need;
-  const int per = (total + kTopkThreads - 1) / kTopkThreads;
-  const int lo = min(total, tid * per);
-  const int hi = min(total, lo + per);
-  int eq_before = 0;
-  if (rank_ties) {
+  const int seg = ((total + kTopkWarps - 1) / kTopkWarps + 31) & ~31;
+  const int lo = min(total, warp * seg);
+  const int hi = min(total, lo + seg);
+  int eq_rank = 0;
+  if (rank_ties) {  // keys equal to the threshold in the warps before this one
     int c = 0;
-    for (int i = lo; i < hi; ++i) c += s_key[i] == prefix ? 1 : 0;
-    int unused;
-    eq_before = cta_scan(c, lane, warp, s_scan, &unused);
-  }
-  // Count pass; each entry's key slot (this thread's own entries, keys no
-  // longer needed) then holds its flags: bit 0 selected, bit 1 valid.
-  int nsel = 0, nvalid = 0;
-  {
-    int eq_rank = eq_before;
-    for (int i = lo; i < hi; ++i) {
-      bool sel = true;
-      if (!all_selected) {
-        const uint32_t key = s_key[i];
-        sel = key > prefix;
-        if (key == prefix) sel = !rank_ties || eq_rank++ < need;
-      }
-      uint32_t flags = 0u;
-      if (sel) {
-        ++nsel;
-        uint32_t lb, local;
-        const int32_t pos = implicit ? i : s_pos[i];
-        const bool valid = owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local);
-        nvalid += valid ? 1 : 0;
-        flags = valid ? 3u : 1u;
-      }
-      s_key[i] = flags;
+    for (int i0 = lo; i0 < hi; i0 += 32) {
+      const int i = i0 + lane;
+      c += __popc(__ballot_sync(kAll, i < hi && s_key[i] == prefix));
     }
+    if (lane == 0) s_scan[warp] = c;
+    __syncthreads();
+    const int w = lane < kTopkWarps ? s_scan[lane] : 0;
+    eq_rank = __reduce_add_sync(kAll, lane < warp ? w : 0);
   }
-  // both counts in one scan: selected in the high half, valid in the low
-  int both_total;
-  const int both = cta_scan((nsel << 16) | nvalid, lane, warp, s_scan, &both_total);
+  // Count pass. Each entry's slots then hold its result: s_pos the position
+  // with bit 30 set when selected and bit 29 when valid, s_key (the key is no
+  // longer needed) the physical slot.
+  constexpr int32_t kSel = 1 << 30, kValid = 1 << 29;
+  int nsel = 0, nvalid = 0;  // this warp's
+  for (int i0 = lo; i0 < hi; i0 += 32) {
+    const int i = i0 + lane;
+    const bool in = i < hi;
+    bool sel = in;
+    if (!all_selected) {
+      const uint32_t key = in ? s_key[i] : 0u;
+      const bool eq = in && key == prefix;
+      sel = in && key > prefix;
+      if (rank_ties) {
+        const uint32_t eqb = __ballot_sync(kAll, eq);
+        sel = sel || (eq && eq_rank + __popc(eqb & lt) < need);
+        eq_rank += __popc(eqb);
+      } else {
+        sel = sel || eq;
+      }
+    }
+    bool valid = false;
+    if (sel) {
+      const int32_t pos = implicit ? i : s_pos[i];
+      uint32_t lb, local;
+      valid = owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local);
+      int32_t phys = -1;
+      if (valid) {
+        const int32_t blk = p.stage ? s_table[lb] : __ldg(trow + lb);
+        phys = static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * static_cast<uint32_t>(p.block_size) + local);
+      }
+      s_key[i] = static_cast<uint32_t>(phys);
+      s_pos[i] = pos | kSel | (valid ? kValid : 0);
+    } else if (in) {
+      s_pos[i] = 0;
+    }
+    nsel += __popc(__ballot_sync(kAll, sel));
+    nvalid += __popc(__ballot_sync(kAll, valid));
+  }
+  // both counts in one exchange: selected in the high half, valid in the low
+  __shared__ int s_wsum[kTopkWarps];
+  if (lane == 0) s_wsum[warp] = (nsel << 16) | nvalid;
+  __syncthreads();
+  const int wsum = lane < kTopkWarps ? s_wsum[lane] : 0;
+  const int both = __reduce_add_sync(kAll, lane < warp ? wsum : 0);
+  const int both_total = __reduce_add_sync(kAll, wsum);
   int js = both >> 16, jv = both & 0xffff;
   const int sel_total = both_total >> 16, valid_total = both_total & 0xffff;
   int32_t* prow = p.positions != nullptr ? p.positions + row * k : nullptr;
   int32_t* orow = p.out + row * k;
-  for (int i = lo; i < hi; ++i) {
-    const uint32_t flags = s_key[i];
-    if (!(flags & 1u)) continue;
-    const int32_t pos = implicit ? i : s_pos[i];
-    const bool valid = (flags & 2u) != 0u;
-    int32_t phys = -1;
-    if (valid) {
-      uint32_t lb, local;
-      (void)owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local);
-      const int32_t blk = p.stage ? s_table[lb] : __ldg(trow + lb);
-      phys = static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * static_cast<uint32_t>(p.block_size) + local);
-    }
-    if (prow != nullptr && js < k) prow[js] = pos;
-    if (p.compact) {
-      if (valid) {
-        if (jv < k) orow[jv] = phys;
-        ++jv;
+  for (int i0 = lo; i0 < hi; i0 += 32) {
+    const int i = i0 + lane;
+    const int32_t f = i < hi ? s_pos[i] : 0;
+    const bool sel = (f & kSel) != 0;
+    const bool valid = (f & kValid) != 0;
+    const uint32_t selb = __ballot_sync(kAll, sel);
+    const uint32_t validb = __ballot_sync(kAll, valid);
+    if (sel) {
+      const int s = js + __popc(selb & lt);
+      const int32_t phys = static_cast<int32_t>(s_key[i]);
+      if (prow != nullptr && s < k) prow[s] = f & (kValid - 1);
+      if (p.compact) {
+        const int v = jv + __popc(validb & lt);
+        if (valid && v < k) orow[v] = phys;
+      } else if (s < k) {
+        orow[s] = phys;
       }
-    } else if (js < k) {
-      orow[js] = phys;
     }
-    ++js;
+    js += __popc(selb);
+    jv += __popc(validb);
   }
   const int n_sel = min(sel_total, k);
   if (prow != nullptr) {
