@@ -17,8 +17,9 @@
 //      above the floor) is kept, per 128-column block;
 //   3. gather: every thread owns a run of whole blocks; one CTA scan over
 //      the threads' candidate counts gives each its offset in the list, and it
-//      writes its candidates' positions from the masks, then loads their keys
-//      (L2 hits, eight in flight), feeding the first radix histogram;
+//      writes its candidates' positions from the masks; then all threads load
+//      the keys (L2 hits, eight in flight per lane), feeding the first radix
+//      histogram;
 //   4. select: the three-pass radix select (11, 11 and 10 key bits) over the
 //      list finds the exact threshold key and how many keys equal to it are
 //      taken (the lowest positions);
@@ -326,8 +327,13 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   };
   const int g0 = kSampleEvery * tid;
   const int g1 = g0 + kSampleEvery * kTopkThreads;
+  // The estimate histogram holds 4 values per sampled float4 (padding
+  // included); a row with fewer than `want_sample` of them has no floor to
+  // find, and lists every column.
+  const uint32_t want_sample = static_cast<uint32_t>(k / kSampleEvery + k / (2 * kSampleEvery) + 16);
+  const bool sampled = len > k && 4u * static_cast<uint32_t>((len + 4 * kSampleEvery - 1) / (4 * kSampleEvery)) >= want_sample;
   float4 first[2];
-  if (len > k) {
+  if (sampled) {
     if (4 * g0 < len) first[0] = sample(g0);
     if (4 * g1 < len) first[1] = sample(g1);
   }
@@ -357,20 +363,24 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
     zero_hist(s_hist[0], tid);
     zero_hist(s_hist[1], tid);
     __syncthreads();
-    auto count = [&](const float4& v) {
-      atomicAdd(&s_hist[0][order_key(v.x) >> 21], 1u);
-      atomicAdd(&s_hist[0][order_key(v.y) >> 21], 1u);
-      atomicAdd(&s_hist[0][order_key(v.z) >> 21], 1u);
-      atomicAdd(&s_hist[0][order_key(v.w) >> 21], 1u);
-    };
-    if (4 * g0 < len) count(first[0]);
-    if (4 * g1 < len) count(first[1]);
-    for (int g = g1 + kSampleEvery * kTopkThreads; 4 * g < len; g += kSampleEvery * kTopkThreads) count(sample(g));
-    __syncthreads();
-    const uint32_t want_sample = static_cast<uint32_t>(k / kSampleEvery + k / (2 * kSampleEvery) + 16);
-    const uint32_t lo_bin = pick_bin(s_hist[0], want_sample, tid, lane, warp, s_scan, s_pick) ? s_pick[0] : 0u;
+    uint32_t lo_bin = 0u;
+    if (sampled) {
+      auto count = [&](const float4& v) {
+        atomicAdd(&s_hist[0][order_key(v.x) >> 21], 1u);
+        atomicAdd(&s_hist[0][order_key(v.y) >> 21], 1u);
+        atomicAdd(&s_hist[0][order_key(v.z) >> 21], 1u);
+        atomicAdd(&s_hist[0][order_key(v.w) >> 21], 1u);
+      };
+      if (4 * g0 < len) count(first[0]);
+      if (4 * g1 < len) count(first[1]);
+      for (int g = g1 + kSampleEvery * kTopkThreads; 4 * g < len; g += kSampleEvery * kTopkThreads) {
+        count(sample(g));
+      }
+      __syncthreads();
+      lo_bin = pick_bin(s_hist[0], want_sample, tid, lane, warp, s_scan, s_pick) ? s_pick[0] : 0u;
+      zero_hist(s_hist[0], tid);  // the first radix pass's (the barriers below order it)
+    }
     const float floor_value = key_floor(lo_bin << 21);
-    zero_hist(s_hist[0], tid);  // the first radix pass's (the barriers below order it)
 
     // 2. stream the row once, keeping candidate masks
     for (int b0 = warp; b0 < nb; b0 += kTopkWarps * kStreamUnroll) {
@@ -395,22 +405,27 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
     __syncthreads();
 
     // 3. the list in position order: each thread lists the candidates of its
-    // own blocks, then loads their keys (L2 hits, eight in flight), which
-    // feed the first radix histogram
-    int mine;
-    const int first = list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &mine, &total);
+    // own blocks; then all threads load the keys, consecutive entries on
+    // consecutive lanes, eight in flight per lane (L2 hits), which feed the
+    // first radix histogram. (Per-thread key loads would serialise on dense
+    // blocks: a short row, or heavy ties, lists every column.)
+    int unused;
+    (void)list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &unused, &total);
     bool whole_row = total > p.cap;
     if (!whole_row) {
-      for (int i0 = first; i0 < first + mine; i0 += 8) {
+      __syncthreads();  // publishes s_pos
+      for (int i0 = tid; i0 < total; i0 += 8 * kTopkThreads) {
         uint32_t kk[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          kk[u] = i0 + u < first + mine ? order_key(__ldg(lrow + s_pos[i0 + u])) : 0u;
+          const int i = i0 + u * kTopkThreads;
+          kk[u] = i < total ? order_key(__ldg(lrow + s_pos[i])) : 0u;
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          if (i0 + u < first + mine) {
-            s_key[i0 + u] = kk[u];
+          const int i = i0 + u * kTopkThreads;
+          if (i < total) {
+            s_key[i] = kk[u];
             atomicAdd(&s_hist[0][kk[u] >> 21], 1u);
           }
         }
@@ -517,7 +532,6 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         if (lane == 0) s_mask[b] = make_uint4(w[0], w[1], w[2], w[3]);
       }
       __syncthreads();
-      int unused;
       (void)list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &unused, &total);
       total = total < p.cap ? total : p.cap;  // exactly top_k <= cap
     }
