@@ -1,7 +1,7 @@
 """Benchmark of the localization converter on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton|vllm|fused|atomic]
-                    [--config C]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--impl ours|reference|triton|vllm|fused|atomic|link] [--config C] [--batch B]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
 
 Default workload (config 3, one step = one converter call): a selection batch
@@ -34,8 +34,9 @@ present under baseline/_ref (a comparison arm; not part of the product).
 ``--impl vllm`` times vLLM's own non-DCP converter beside ours on the
 workload's shapes at dcp_size 1, where the two compute the same function.
 ``--impl fused`` times the fused indexer top-k + localization kernel on
-256 x 65536 logits (top_k 2048, dcp 4) beside vLLM's top-k followed by the
-converter.
+256 x 65536 logits (top_k 2048, dcp 4; ``--batch`` sets the rows) beside
+vLLM's top-k followed by the converter. ``--impl link`` times the end-to-end
+step's host copies alone, the host link's ceiling for ``e2e``.
 """
 
 from __future__ import annotations
@@ -684,6 +685,99 @@ def run_fused(args, rank: int, world: int) -> dict | None:
     }
 
 
+def run_link(args, rank: int, world: int) -> dict | None:
+    """The host link's ceiling for the end-to-end line: its copies alone.
+
+    Per step, the end-to-end arm moves the workload's inputs to the device
+    (one H2D copy per call: req_ids, table and tokens) and its results back
+    (two D2H copies per call: out and counts) from pinned host buffers. This
+    arm times those same copies with no kernel: H2D alone, D2H alone, and both
+    directions at once on two streams, which bounds the end-to-end step from
+    below. A comparison arm, rank 0 only; no localization runs.
+    """
+    if rank != 0:
+        return None
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    calls = WORKLOADS[args.config]["calls"]
+    case = _case(args.config, seed=0, dcp_rank=0)
+    n_in = case.req_ids.size + case.block_table.size + case.tokens.size
+    n_out = case.tokens.size
+    pairs = []
+    for _ in range(2 * calls):  # two buffer sets per call, alternating
+        pairs.append((torch.empty(n_in, dtype=torch.int32).pin_memory(),
+                      torch.empty(n_in, dtype=torch.int32, device=dev),
+                      torch.empty(n_out, dtype=torch.int32, device=dev),
+                      torch.empty(n_out, dtype=torch.int32).pin_memory(),
+                      torch.empty(case.batch, dtype=torch.int32, device=dev),
+                      torch.empty(case.batch, dtype=torch.int32).pin_memory()))
+    streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
+    steps = max(1, min(args.steps, 200))
+
+    def h2d(stream, step):
+        with torch.cuda.stream(stream):
+            for c in range(calls):
+                host_in, dev_in = pairs[(step % 2) * calls + c][:2]
+                dev_in.copy_(host_in, non_blocking=True)
+
+    def d2h(stream, step):
+        with torch.cuda.stream(stream):
+            for c in range(calls):
+                _, _, dev_out, host_out, dev_counts, host_counts = pairs[(step % 2) * calls + c]
+                host_out.copy_(dev_out, non_blocking=True)
+                host_counts.copy_(dev_counts, non_blocking=True)
+
+    def timed(directions) -> float:
+        """Seconds per step, the best of three runs after a warm-up."""
+        current = torch.cuda.current_stream(dev)
+        for step in range(max(3, args.warmup)):
+            for fn, stream in zip(directions, streams):
+                fn(stream, step)
+        torch.cuda.synchronize(dev)
+        best = math.inf
+        for _ in range(3):
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(current)
+            for stream in streams:
+                stream.wait_event(start)
+            for step in range(steps):
+                for fn, stream in zip(directions, streams):
+                    fn(stream, step)
+            for stream in streams:
+                current.wait_stream(stream)
+            end.record(current)
+            torch.cuda.synchronize(dev)
+            best = min(best, start.elapsed_time(end) / 1e3 / steps)
+        return best
+
+    h2d_bytes = 4 * n_in * calls
+    d2h_bytes = 4 * (n_out + case.batch) * calls
+    t_in = timed([h2d])
+    t_out = timed([d2h])
+    t_both = timed([h2d, d2h])
+    return {
+        "impl": "host-link",
+        "metric": "us per step, the end-to-end step's host copies alone (no kernel)",
+        "unit": "us/step",
+        "higher_is_better": False,
+        "steps": steps,
+        "h2d_bytes_per_step": h2d_bytes,
+        "d2h_bytes_per_step": d2h_bytes,
+        "h2d_us_per_step": t_in * 1e6,
+        "d2h_us_per_step": t_out * 1e6,
+        "both_us_per_step": t_both * 1e6,
+        "value": t_both * 1e6,
+        "h2d_gbs": h2d_bytes / t_in / 1e9,
+        "d2h_gbs": d2h_bytes / t_out / 1e9,
+        "both_gbs": (h2d_bytes + d2h_bytes) / t_both / 1e9,
+        "config": {"workload": WORKLOADS[args.config]["desc"], "buffers": "pinned host, two sets alternating"},
+        "data": "synthetic",
+    }
+
+
 def _make_call(arm: str, bufs: dict, geometry: dict, tile_size: int):
     from silkern_b200.baselines import launch_atomic_baseline
     from silkern_b200.kernels import localize_hierarchical, localize_rowwise
@@ -982,7 +1076,7 @@ def main(argv=None) -> int:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=2000)
     parser.add_argument("--warmup", type=int, default=64)
-    parser.add_argument("--impl", choices=["ours", "reference", "triton", "vllm", "fused", "atomic"],
+    parser.add_argument("--impl", choices=["ours", "reference", "triton", "vllm", "fused", "atomic", "link"],
                         default="ours")
     parser.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=3)
     parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
@@ -996,9 +1090,9 @@ def main(argv=None) -> int:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
-    if args.impl in ("reference", "triton", "vllm", "fused"):
+    if args.impl in ("reference", "triton", "vllm", "fused", "link"):
         result = {"reference": run_reference, "triton": run_triton, "vllm": run_vllm,
-                  "fused": run_fused}[args.impl](args, rank, world)
+                  "fused": run_fused, "link": run_link}[args.impl](args, rank, world)
         if result is not None:
             print(json.dumps(result), flush=True)
         return 0
