@@ -349,9 +349,11 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   }
 
   // The list: `total` entries in position order holding every selected
-  // position. `prefix` is the threshold key, `need` how many keys equal to it
-  // are taken, `eq_total` how many there are; `all_selected` when the list is
-  // exactly the selection (short rows, and the whole-row path).
+  // position. `prefix` is the threshold key: when `need` equals `eq_total`
+  // every key at or above it is taken, otherwise every key above it and the
+  // `need` lowest-positioned of the `eq_total` keys equal to it.
+  // `all_selected` when the list is exactly the selection (short rows, and
+  // the whole-row path).
   int total = 0;
   uint32_t prefix = 0;
   int need = 0;
@@ -434,7 +436,10 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
 
       // 4. exact radix select over the list (first pass counted above). The
       // passes alternate histograms: each pass clears the one the next uses.
+      // A pass whose threshold bin is taken whole ends the select; `prefix`
+      // then becomes the bin's lowest key.
       need = k;
+      int rest = 0;
 #pragma unroll 1
       for (int pass = 0; pass < 3; ++pass) {
         const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
@@ -456,7 +461,10 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         prefix = (prefix << bits) | s_pick[0];
         need -= static_cast<int>(s_pick[1]);
         eq_total = static_cast<int>(s_pick[2]);
+        rest = shift;
+        if (eq_total == need) break;
       }
+      prefix <<= rest;
       all_selected = whole_row;
     }
 
@@ -466,6 +474,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
       // positioned keys equal to it.
       prefix = 0;
       need = k;
+      int rest = 0;
 #pragma unroll 1
       for (int pass = 0; pass < 3; ++pass) {
         const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
@@ -489,7 +498,10 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         prefix = (prefix << bits) | s_pick[0];
         need -= static_cast<int>(s_pick[1]);
         eq_total = static_cast<int>(s_pick[2]);
+        rest = shift;
+        if (eq_total == need) break;  // the threshold bin is taken whole
       }
+      prefix <<= rest;  // the lowest key taken when no tie is cut
       const bool tie_cut = eq_total != need;
       if (tie_cut) {
         // masks of the keys equal to the threshold, and their block offsets

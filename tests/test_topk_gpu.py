@@ -117,6 +117,49 @@ def test_internal_paths(capacity, stage, kind) -> None:
     assert np.array_equal(pos, want[0]) and np.array_equal(out, want[1]) and np.array_equal(counts, want[2])
 
 
+def _bin_taken_whole_rows(rng, last_pass, batch, width, top_k):
+    """Rows whose radix select ends at `last_pass` because the threshold bin
+    there holds exactly the keys still needed. Order keys split 11/11/10 bits:
+    an 11-bit bin spans [1024, 1280) at exponent 10, a 22-bit bin 0.125 there.
+    """
+    logits = rng.standard_normal((batch, width)).astype(np.float32)  # all below 10
+    for r in range(batch):
+        cols = rng.permutation(width)
+        if last_pass == 0:
+            # top_k distinct scores alone in [1024, 1280)
+            logits[r, cols[:top_k]] = rng.uniform(1024.0, 1279.0, size=top_k)
+        elif last_pass == 1:
+            # top_k - 10 high scores; the threshold's 11-bit bin holds 30, of
+            # which 10 share the top 22-bit bin [1100, 1100.125)
+            logits[r, cols[:top_k - 10]] = rng.uniform(2048.0, 2559.0, size=top_k - 10)
+            logits[r, cols[top_k - 10:top_k]] = 1100.0 + 0.01 * np.arange(10)
+            logits[r, cols[top_k:top_k + 20]] = rng.uniform(1030.0, 1090.0, size=20)
+        else:
+            # the 22-bit bin [1100, 1100.125) holds 12 with 8 needed: 3 above
+            # the threshold and exactly 5 equal to it, taken with no tie cut
+            logits[r, cols[:top_k - 8]] = rng.uniform(2048.0, 2559.0, size=top_k - 8)
+            logits[r, cols[top_k - 8:top_k - 5]] = 1100.0625
+            logits[r, cols[top_k - 5:top_k]] = 1100.03
+            logits[r, cols[top_k:top_k + 4]] = 1100.0
+    return logits
+
+
+@pytest.mark.parametrize("capacity", [0, 1000], ids=["list", "whole_row"])
+@pytest.mark.parametrize("last_pass", [0, 1, 2])
+def test_threshold_bin_taken_whole(last_pass, capacity) -> None:
+    """The select ends early when a pass's threshold bin is taken whole."""
+    width, top_k, batch = 20000, 1000, 3
+    rng = np.random.default_rng(7330 + last_pass)
+    logits = _bin_taken_whole_rows(rng, last_pass, batch, width, top_k)
+    lens = np.full(batch, width, dtype=np.int32)
+    table = _table(rng, batch, 400)
+    req = np.arange(batch, dtype=np.int32)
+    kw = dict(block_size=64, dcp_size=2, dcp_rank=1)
+    pos, out, counts = _run(_dev(logits), lens, req, table, top_k, candidate_capacity=capacity, **kw)
+    want = oracle_topk(logits, lens, req, table, top_k=top_k, **kw)
+    assert np.array_equal(pos, want[0]) and np.array_equal(out, want[1]) and np.array_equal(counts, want[2])
+
+
 def test_estimate_misses_fall_back_exactly() -> None:
     """Rows whose sampled columns are unrepresentative: 1000 of the sampled
     float4 groups' columns score high, so the floor lands above all but those
