@@ -577,12 +577,17 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   // longer needed) the physical slot.
   constexpr int32_t kSel = 1 << 30, kValid = 1 << 29;
   int nsel = 0, nvalid = 0;  // this warp's
+#pragma unroll 2
   for (int i0 = lo; i0 < hi; i0 += 32) {
+    // branch-free: every lane reads an entry of the list (lanes past the
+    // end re-read the first) and computes its ownership and slot
     const int i = i0 + lane;
     const bool in = i < hi;
+    const int ic = in ? i : lo;
+    const int32_t pos = implicit ? ic : s_pos[ic];
     bool sel = in;
     if (!all_selected) {
-      const uint32_t key = in ? s_key[i] : 0u;
+      const uint32_t key = s_key[ic];
       const bool eq = in && key == prefix;
       sel = in && key > prefix;
       if (rank_ties) {
@@ -593,20 +598,17 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         sel = sel || eq;
       }
     }
-    bool valid = false;
-    if (sel) {
-      const int32_t pos = implicit ? i : s_pos[i];
-      uint32_t lb, local;
-      valid = owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local);
-      int32_t phys = -1;
-      if (valid) {
-        const int32_t blk = p.stage ? s_table[lb] : __ldg(trow + lb);
-        phys = static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * static_cast<uint32_t>(p.block_size) + local);
-      }
+    uint32_t lb, local;
+    const bool own = owned(p, static_cast<uint32_t>(pos), twidth, &lb, &local);
+    const bool valid = sel && own;
+    const uint32_t lbc = own ? lb : 0u;  // an entry of the row (read, unused, when not owned)
+    const int32_t blk = p.stage ? s_table[lbc] : __ldg(trow + lbc);
+    const int32_t phys =
+        valid ? static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * static_cast<uint32_t>(p.block_size) + local)
+              : -1;
+    if (in) {
       s_key[i] = static_cast<uint32_t>(phys);
-      s_pos[i] = pos | kSel | (valid ? kValid : 0);
-    } else if (in) {
-      s_pos[i] = 0;
+      s_pos[i] = sel ? (pos | kSel | (valid ? kValid : 0)) : 0;
     }
     nsel += __popc(__ballot_sync(kAll, sel));
     nvalid += __popc(__ballot_sync(kAll, valid));
@@ -622,23 +624,23 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
   const int sel_total = both_total >> 16, valid_total = both_total & 0xffff;
   int32_t* prow = p.positions != nullptr ? p.positions + row * k : nullptr;
   int32_t* orow = p.out + row * k;
+#pragma unroll 2
   for (int i0 = lo; i0 < hi; i0 += 32) {
     const int i = i0 + lane;
-    const int32_t f = i < hi ? s_pos[i] : 0;
+    const bool in = i < hi;
+    const int32_t f = in ? s_pos[i] : 0;
+    const int32_t phys = static_cast<int32_t>(s_key[in ? i : lo]);
     const bool sel = (f & kSel) != 0;
     const bool valid = (f & kValid) != 0;
     const uint32_t selb = __ballot_sync(kAll, sel);
     const uint32_t validb = __ballot_sync(kAll, valid);
-    if (sel) {
-      const int s = js + __popc(selb & lt);
-      const int32_t phys = static_cast<int32_t>(s_key[i]);
-      if (prow != nullptr && s < k) prow[s] = f & (kValid - 1);
-      if (p.compact) {
-        const int v = jv + __popc(validb & lt);
-        if (valid && v < k) orow[v] = phys;
-      } else if (s < k) {
-        orow[s] = phys;
-      }
+    const int s = js + __popc(selb & lt);
+    const int v = jv + __popc(validb & lt);
+    if (prow != nullptr && sel && s < k) prow[s] = f & (kValid - 1);
+    if (p.compact) {
+      if (valid && v < k) orow[v] = phys;
+    } else if (sel && s < k) {
+      orow[s] = phys;
     }
     js += __popc(selb);
     jv += __popc(validb);
