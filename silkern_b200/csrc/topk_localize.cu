@@ -235,10 +235,11 @@ __device__ __forceinline__ void block_offsets(const uint4* s_mask, int32_t* s_bo
 // Lays the set bits of the blocks' masks (s_mask, `nb` blocks) out in
 // position order: thread t owns a contiguous run of whole blocks, one CTA scan
 // gives its first list index, and it writes the positions of its own set bits
-// (those below `cap`). Returns that first index; *mine gets the thread's count
-// and *total the CTA's. Contains the scan's barriers; every thread must call it.
-__device__ __forceinline__ int list_positions(const uint4* s_mask, int nb, int tid, int lane, int warp,
-                                              int* s_scan, int32_t* s_pos, int cap, int* mine, int* total) {
+// (those below `cap`); *total gets the CTA's count. Contains the scan's
+// barriers; every thread must call it. The positions are published by the
+// caller's next barrier.
+__device__ __forceinline__ void list_positions(const uint4* s_mask, int nb, int tid, int lane, int warp,
+                                               int* s_scan, int32_t* s_pos, int cap, int* total) {
   const int per = (nb + kTopkThreads - 1) / kTopkThreads;
   const int b_lo = min(nb, tid * per);
   const int b_hi = min(nb, b_lo + per);
@@ -267,8 +268,6 @@ __device__ __forceinline__ int list_positions(const uint4* s_mask, int nb, int t
       idx += (m.w >> l) & 1u;
     }
   }
-  *mine = c;
-  return first;
 }
 
 __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __grid_constant__ TopkParams p) {
@@ -411,8 +410,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
     // consecutive lanes, eight in flight per lane (L2 hits), which feed the
     // first radix histogram. (Per-thread key loads would serialise on dense
     // blocks: a short row, or heavy ties, lists every column.)
-    int unused;
-    (void)list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &unused, &total);
+    list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &total);
     bool whole_row = total > p.cap;
     if (!whole_row) {
       __syncthreads();  // publishes s_pos
@@ -544,7 +542,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         if (lane == 0) s_mask[b] = make_uint4(w[0], w[1], w[2], w[3]);
       }
       __syncthreads();
-      (void)list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &unused, &total);
+      list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &total);
       total = total < p.cap ? total : p.cap;  // exactly top_k <= cap
     }
   } else {
