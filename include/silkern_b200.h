@@ -240,6 +240,22 @@ int silkern_topk_localize_explicit_v1(const float* logits, int64_t logits_stride
                                       int32_t candidate_capacity, int32_t stage_table,
                                       int32_t* status, void* stream);
 
+/*
+ * silkern_topk_localize_explicit_v1 with the CTA shape pinned as well:
+ * cta_threads 0 (automatic: 1024 threads, one CTA per SM, when batch is at
+ * most the device's SM count, else 512 threads, two per SM), 512 or 1024.
+ * SILKERN_E_GEOMETRY for any other value.
+ */
+int silkern_topk_localize_explicit_v2(const float* logits, int64_t logits_stride,
+                                      int64_t logits_width, const int32_t* seq_lens,
+                                      const int32_t* req_ids, const int32_t* block_table,
+                                      int64_t table_rows, int64_t table_width, int32_t* positions,
+                                      int32_t* out, int32_t* counts, int64_t batch, int32_t top_k,
+                                      int32_t block_size, int32_t dcp_size, int32_t dcp_rank,
+                                      int32_t dcp_interleave, int32_t compact_valid_to_front,
+                                      int32_t candidate_capacity, int32_t stage_table,
+                                      int32_t cta_threads, int32_t* status, void* stream);
+
 /* Static text for a return code (positive SILKERN_E*, 0, or -cudaError_t). */
 const char* silkern_status_string_v1(int code);
 

@@ -59,6 +59,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_ptr, _i64, _i64, _ptr, _ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _i64, _i32, _i32, _i32,
          _i32, _i32, _i32, _i32, _i32, _ptr, _ptr],
     ),
+    "silkern_topk_localize_explicit_v2": (
+        _i32,
+        [_ptr, _i64, _i64, _ptr, _ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _i64, _i32, _i32, _i32,
+         _i32, _i32, _i32, _i32, _i32, _i32, _ptr, _ptr],
+    ),
     "silkern_status_string_v1": (ctypes.c_char_p, [ctypes.c_int]),
     "silkern_abi_version_v1": (ctypes.c_int, []),
     "silkern_fastdiv_selftest_v1": (_i64, [_u32, _u32, _u32]),

@@ -52,20 +52,22 @@
 namespace silkern {
 namespace {
 
-constexpr int kTopkThreads = 512;
-constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kBlockCols = 128;  // one float4 per lane of a warp
 constexpr int kBins = 2048;      // 11-bit radix digit
-constexpr int kBinsPerThread = kBins / kTopkThreads;
 constexpr int kSampleEvery = 16;      // one float4 of every 16 feeds the estimate
 constexpr int64_t kPrefetchBytes = 16384;  // per bulk L2 prefetch
 constexpr int kStreamUnroll = 8;      // 128-column blocks in flight per warp
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
 constexpr int64_t kTopkSmemBudget = 200 * 1024;  // dynamic shared memory per CTA
 constexpr int kMaxBlocks = SILKERN_TOPK_MAX_WIDTH / kBlockCols;
-constexpr int kBlocksPerThread = kMaxBlocks / kTopkThreads;
 constexpr uint32_t kAll = 0xffffffffu;
-static_assert(kBinsPerThread == 4 && kBlocksPerThread == 4, "per-thread shares of bins and blocks");
+// CTA shapes (threads T): 512 threads, two CTAs per SM, when the batch needs
+// more than one CTA per SM; 1024 threads, one per SM, when every row has an
+// SM of its own. Per thread: kBins / T histogram bins, kMaxBlocks / T blocks.
+constexpr int kSmallCta = 512;
+constexpr int kLargeCta = 1024;
+static_assert(kBins / kLargeCta == 2 && kBins / kSmallCta == 4, "per-thread shares of the histogram bins");
+static_assert(kMaxBlocks % kLargeCta == 0, "per-thread shares of the blocks");
 
 struct TopkParams {
   const float* logits;
@@ -116,8 +118,9 @@ __device__ __forceinline__ bool owned(const TopkParams& p, uint32_t u, uint32_t 
   return q1 - q2 * p.dcp_size == p.dcp_rank && *lb < twidth;
 }
 
-// Exclusive prefix of v over the CTA in thread order; *total gets the sum.
-// Contains two barriers; every thread of the CTA must call it.
+// Exclusive prefix of v over the CTA (T threads) in thread order; *total gets
+// the sum. Contains two barriers; every thread of the CTA must call it.
+template <int T>
 __device__ __forceinline__ int cta_scan(int v, int lane, int warp, int* s_scan, int* total) {
   int x = v;
 #pragma unroll
@@ -127,7 +130,7 @@ __device__ __forceinline__ int cta_scan(int v, int lane, int warp, int* s_scan, 
   }
   if (lane == 31) s_scan[warp] = x;
   __syncthreads();
-  const int w = lane < kTopkWarps ? s_scan[lane] : 0;
+  const int w = lane < T / 32 ? s_scan[lane] : 0;
   int wi = w;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -141,9 +144,10 @@ __device__ __forceinline__ int cta_scan(int v, int lane, int warp, int* s_scan, 
 }
 
 // Zero a histogram; a later barrier orders it before the next fill.
+template <int T>
 __device__ __forceinline__ void zero_hist(uint32_t* hist, int tid) {
 #pragma unroll
-  for (int b = 0; b < kBinsPerThread; ++b) hist[b * kTopkThreads + tid] = 0u;
+  for (int b = 0; b < kBins / T; ++b) hist[b * T + tid] = 0u;
 }
 
 // The histogram is complete (the caller's barrier). Returns whether its total
@@ -151,11 +155,25 @@ __device__ __forceinline__ void zero_hist(uint32_t* hist, int tid) {
 // counted from the top, first reaches `want` is published as s_pick = {bin,
 // count above it, count in it}. Ends with a barrier. (s_pick is written only
 // after the first barrier here, when every thread has read the last pick.)
+template <int T>
 __device__ __forceinline__ bool pick_bin(const uint32_t* hist, uint32_t want, int tid, int lane, int warp,
                                          int* s_scan, uint32_t* s_pick) {
-  const uint4 hv = *reinterpret_cast<const uint4*>(hist + kBinsPerThread * tid);
-  const uint32_t h[kBinsPerThread] = {hv.x, hv.y, hv.z, hv.w};
-  const uint32_t mine = h[0] + h[1] + h[2] + h[3];
+  constexpr int kPer = kBins / T;  // this thread's bins: kPer * tid ..
+  uint32_t h[kPer];
+  if constexpr (kPer == 4) {
+    const uint4 hv = *reinterpret_cast<const uint4*>(hist + kPer * tid);
+    h[0] = hv.x;
+    h[1] = hv.y;
+    h[2] = hv.z;
+    h[3] = hv.w;
+  } else {
+    const uint2 hv = *reinterpret_cast<const uint2*>(hist + kPer * tid);
+    h[0] = hv.x;
+    h[1] = hv.y;
+  }
+  uint32_t mine = 0u;
+#pragma unroll
+  for (int b = 0; b < kPer; ++b) mine += h[b];
   // count in the bins of higher threads: suffix over lanes, then warps
   uint32_t suffix = mine;
 #pragma unroll
@@ -165,15 +183,15 @@ __device__ __forceinline__ bool pick_bin(const uint32_t* hist, uint32_t want, in
   }
   if (lane == 0) s_scan[warp] = static_cast<int>(suffix);
   __syncthreads();
-  const uint32_t wt = lane < kTopkWarps ? static_cast<uint32_t>(s_scan[lane]) : 0u;
+  const uint32_t wt = lane < T / 32 ? static_cast<uint32_t>(s_scan[lane]) : 0u;
   const uint32_t above = suffix - mine + __reduce_add_sync(kAll, lane > warp ? wt : 0u);
   const uint32_t all = __reduce_add_sync(kAll, wt);
   if (above < want && want <= above + mine) {
     uint32_t a = above;
 #pragma unroll
-    for (int b = kBinsPerThread - 1; b >= 0; --b) {
+    for (int b = kPer - 1; b >= 0; --b) {
       if (a + h[b] >= want) {
-        s_pick[0] = static_cast<uint32_t>(kBinsPerThread * tid + b);
+        s_pick[0] = static_cast<uint32_t>(kPer * tid + b);
         s_pick[1] = a;
         s_pick[2] = h[b];
         break;
@@ -207,14 +225,16 @@ __device__ __forceinline__ int rank_in_block(const uint32_t m[4], uint32_t lt, i
 }
 
 // s_boff[b] = list offset of block b (masks in s_mask, in block order), over
-// `nb` blocks, four per thread; *total gets the number of set bits.
+// `nb` blocks, kMaxBlocks / T per thread; *total gets the number of set bits.
+template <int T>
 __device__ __forceinline__ void block_offsets(const uint4* s_mask, int32_t* s_boff, int nb, int tid, int lane,
                                               int warp, int* s_scan, int* total) {
-  int c[kBlocksPerThread];
+  constexpr int kPer = kMaxBlocks / T;
+  int c[kPer];
   int mine = 0;
 #pragma unroll
-  for (int i = 0; i < kBlocksPerThread; ++i) {
-    const int b = kBlocksPerThread * tid + i;
+  for (int i = 0; i < kPer; ++i) {
+    const int b = kPer * tid + i;
     c[i] = 0;
     if (b < nb) {
       const uint4 m = s_mask[b];
@@ -222,10 +242,10 @@ __device__ __forceinline__ void block_offsets(const uint4* s_mask, int32_t* s_bo
     }
     mine += c[i];
   }
-  int run = cta_scan(mine, lane, warp, s_scan, total);
+  int run = cta_scan<T>(mine, lane, warp, s_scan, total);
 #pragma unroll
-  for (int i = 0; i < kBlocksPerThread; ++i) {
-    const int b = kBlocksPerThread * tid + i;
+  for (int i = 0; i < kPer; ++i) {
+    const int b = kPer * tid + i;
     if (b < nb) s_boff[b] = run;
     run += c[i];
   }
@@ -238,9 +258,10 @@ __device__ __forceinline__ void block_offsets(const uint4* s_mask, int32_t* s_bo
 // (those below `cap`); *total gets the CTA's count. Contains the scan's
 // barriers; every thread must call it. The positions are published by the
 // caller's next barrier.
+template <int T>
 __device__ __forceinline__ void list_positions(const uint4* s_mask, int nb, int tid, int lane, int warp,
                                                int* s_scan, int32_t* s_pos, int cap, int* total) {
-  const int per = (nb + kTopkThreads - 1) / kTopkThreads;
+  const int per = (nb + T - 1) / T;
   const int b_lo = min(nb, tid * per);
   const int b_hi = min(nb, b_lo + per);
   int c = 0;
@@ -248,7 +269,7 @@ __device__ __forceinline__ void list_positions(const uint4* s_mask, int nb, int 
     const uint4 m = s_mask[b];
     c += __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w);
   }
-  const int first = cta_scan(c, lane, warp, s_scan, total);
+  const int first = cta_scan<T>(c, lane, warp, s_scan, total);
   int idx = first;
   for (int b = b_lo; b < b_hi; ++b) {
     const uint4 m = s_mask[b];
@@ -270,7 +291,10 @@ __device__ __forceinline__ void list_positions(const uint4* s_mask, int nb, int 
   }
 }
 
-__global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __grid_constant__ TopkParams p) {
+template <int T>
+__global__ void __launch_bounds__(T, T == kSmallCta ? 2 : 1) topk_localize_kernel(const __grid_constant__ TopkParams p) {
+  constexpr int kTopkThreads = T;
+  constexpr int kTopkWarps = T / 32;
   extern __shared__ __align__(16) unsigned char smem[];
   uint4* s_mask = reinterpret_cast<uint4*>(smem);  // per 128-column block: bit l of word j = column 4l + j
   int32_t* s_boff = reinterpret_cast<int32_t*>(smem + p.off_boff);  // list offset per block
@@ -361,8 +385,8 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
 
   if (len > k) {
     // 1. estimate from every 16th float4
-    zero_hist(s_hist[0], tid);
-    zero_hist(s_hist[1], tid);
+    zero_hist<T>(s_hist[0], tid);
+    zero_hist<T>(s_hist[1], tid);
     __syncthreads();
     uint32_t lo_bin = 0u;
     if (sampled) {
@@ -378,8 +402,8 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         count(sample(g));
       }
       __syncthreads();
-      lo_bin = pick_bin(s_hist[0], want_sample, tid, lane, warp, s_scan, s_pick) ? s_pick[0] : 0u;
-      zero_hist(s_hist[0], tid);  // the first radix pass's (the barriers below order it)
+      lo_bin = pick_bin<T>(s_hist[0], want_sample, tid, lane, warp, s_scan, s_pick) ? s_pick[0] : 0u;
+      zero_hist<T>(s_hist[0], tid);  // the first radix pass's (the barriers below order it)
     }
     const float floor_value = key_floor(lo_bin << 21);
 
@@ -410,7 +434,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
     // consecutive lanes, eight in flight per lane (L2 hits), which feed the
     // first radix histogram. (Per-thread key loads would serialise on dense
     // blocks: a short row, or heavy ties, lists every column.)
-    list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &total);
+    list_positions<T>(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &total);
     bool whole_row = total > p.cap;
     if (!whole_row) {
       __syncthreads();  // publishes s_pos
@@ -444,14 +468,14 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         const int bits = pass == 2 ? 10 : 11;
         uint32_t* hist = s_hist[pass & 1];
         if (pass > 0) {
-          if (pass == 1) zero_hist(s_hist[0], tid);
+          if (pass == 1) zero_hist<T>(s_hist[0], tid);
           for (int i = tid; i < total; i += kTopkThreads) {
             const uint32_t key = s_key[i];
             if ((key >> (shift + bits)) == prefix) atomicAdd(&hist[(key >> shift) & (kBins - 1)], 1u);
           }
           __syncthreads();
         }
-        const bool found = pick_bin(hist, static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
+        const bool found = pick_bin<T>(hist, static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
         if (pass == 0 && !(found && s_pick[0] >= lo_bin)) {
           whole_row = true;  // fewer than top_k scores above the floor
           break;
@@ -477,7 +501,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
       for (int pass = 0; pass < 3; ++pass) {
         const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
         const int bits = pass == 2 ? 10 : 11;
-        zero_hist(s_hist[0], tid);
+        zero_hist<T>(s_hist[0], tid);
         __syncthreads();
         for (int b = warp; b < nb; b += kTopkWarps) {
           const float4 v = load_block(lrow, b, lane, len, vec);
@@ -492,7 +516,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
           }
         }
         __syncthreads();
-        (void)pick_bin(s_hist[0], static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
+        (void)pick_bin<T>(s_hist[0], static_cast<uint32_t>(need), tid, lane, warp, s_scan, s_pick);
         prefix = (prefix << bits) | s_pick[0];
         need -= static_cast<int>(s_pick[1]);
         eq_total = static_cast<int>(s_pick[2]);
@@ -514,7 +538,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         }
         __syncthreads();
         int eqs;
-        block_offsets(s_mask, s_boff, nb, tid, lane, warp, s_scan, &eqs);
+        block_offsets<T>(s_mask, s_boff, nb, tid, lane, warp, s_scan, &eqs);
       }
       // selection masks (each warp rewrites only the blocks it read)
       for (int b = warp; b < nb; b += kTopkWarps) {
@@ -542,7 +566,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_localize_kernel(const __
         if (lane == 0) s_mask[b] = make_uint4(w[0], w[1], w[2], w[3]);
       }
       __syncthreads();
-      list_positions(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &total);
+      list_positions<T>(s_mask, nb, tid, lane, warp, s_scan, s_pos, p.cap, &total);
       total = total < p.cap ? total : p.cap;  // exactly top_k <= cap
     }
   } else {
@@ -661,25 +685,52 @@ bool byte_overlap(const void* a, int64_t a_bytes, const void* b, int64_t b_bytes
   return a0 < b0 + static_cast<uintptr_t>(b_bytes) && b0 < a0 + static_cast<uintptr_t>(a_bytes);
 }
 
-// Dynamic shared memory above the default needs an opt-in per kernel and
-// device; the largest size granted so far is remembered.
-int allow_topk_smem(size_t bytes) {
-  static std::mutex mutex;
-  static size_t granted[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
+// Per device: the SM count, and the dynamic shared memory granted so far to
+// each CTA shape's kernel (above the default it needs an opt-in per kernel
+// and device).
+struct TopkDevice {
+  int sms = 0;
+  size_t granted[2] = {0, 0};  // 512- and 1024-thread kernels
+};
+
+int topk_device(int* dev, TopkDevice** out) {
+  static TopkDevice devices[64];
+  if (cudaGetDevice(dev) != cudaSuccess || *dev < 0 || *dev >= 64) {
     const cudaError_t err = cudaGetLastError();
     return -static_cast<int>(err == cudaSuccess ? cudaErrorInvalidDevice : err);
   }
+  *out = &devices[*dev];
+  return SILKERN_OK;
+}
+
+int topk_prepare(int threads, size_t smem_bytes, int* sms) {
+  static std::mutex mutex;
+  int dev = 0;
+  TopkDevice* d = nullptr;
+  const int rc = topk_device(&dev, &d);
+  if (rc != SILKERN_OK) return rc;
   std::lock_guard<std::mutex> lock(mutex);
-  if (dev >= 0 && dev < 64 && granted[dev] >= bytes) return SILKERN_OK;
-  const cudaError_t err = cudaFuncSetAttribute(topk_localize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(bytes));
+  if (d->sms == 0) {
+    int n = 0;
+    const cudaError_t err = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess) {
+      (void)cudaGetLastError();
+      return -static_cast<int>(err);
+    }
+    d->sms = n;
+  }
+  *sms = d->sms;
+  if (threads == 0) return SILKERN_OK;
+  const int slot = threads == kLargeCta ? 1 : 0;
+  if (d->granted[slot] >= smem_bytes) return SILKERN_OK;
+  const cudaError_t err = cudaFuncSetAttribute(
+      threads == kLargeCta ? topk_localize_kernel<kLargeCta> : topk_localize_kernel<kSmallCta>,
+      cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_bytes));
   if (err != cudaSuccess) {
     (void)cudaGetLastError();
     return -static_cast<int>(err);
   }
-  if (dev >= 0 && dev < 64) granted[dev] = bytes;
+  d->granted[slot] = smem_bytes;
   return SILKERN_OK;
 }
 
@@ -689,7 +740,7 @@ int topk_launch(const float* logits, int64_t stride, int64_t width, const int32_
                 const int32_t* req_ids, const int32_t* table, int64_t table_rows, int64_t table_width,
                 int32_t* positions, int32_t* out, int32_t* counts, int64_t batch, int32_t top_k,
                 int32_t block_size, int32_t dcp_size, int32_t dcp_rank, int32_t interleave, int32_t compact,
-                int32_t cap_req, int32_t stage_req, int32_t* status, cudaStream_t stream) {
+                int32_t cap_req, int32_t stage_req, int32_t threads_req, int32_t* status, cudaStream_t stream) {
   if (!logits || !seq_lens || !req_ids || !table || !out || !counts) return SILKERN_E_NULL;
   if (batch < 1 || batch > INT32_MAX || width < 1 || width > SILKERN_TOPK_MAX_WIDTH || stride < width ||
       top_k < 1 || top_k > SILKERN_MAX_ROW_WIDTH || table_rows < 1 || table_width < 1 || table_width > INT32_MAX) {
@@ -745,7 +796,13 @@ int topk_launch(const float* logits, int64_t stride, int64_t width, const int32_
   p.off_pos = p.off_key + align16(cap * 4);
   p.off_table = p.off_pos + align16(cap * 4);
   const int64_t smem = p.off_table + (stage ? align16(table_width * 4) : 0);
-  const int rc = allow_topk_smem(static_cast<size_t>(smem));
+  // CTA shape: 1024 threads when every row gets an SM of its own
+  if (threads_req != 0 && threads_req != kSmallCta && threads_req != kLargeCta) return SILKERN_E_GEOMETRY;
+  int sms = 0;
+  int rc = topk_prepare(0, 0, &sms);
+  if (rc != SILKERN_OK) return rc;
+  const int threads = threads_req != 0 ? threads_req : (batch <= sms ? kLargeCta : kSmallCta);
+  rc = topk_prepare(threads, static_cast<size_t>(smem), &sms);
   if (rc != SILKERN_OK) return rc;
 
   p.logits = logits;
@@ -775,7 +832,7 @@ int topk_launch(const float* logits, int64_t stride, int64_t width, const int32_
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(batch), 1, 1);
-  cfg.blockDim = dim3(kTopkThreads, 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = stream;
   cudaLaunchAttribute attrs[1];
@@ -783,7 +840,8 @@ int topk_launch(const float* logits, int64_t stride, int64_t width, const int32_
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, topk_localize_kernel, p);
+  const cudaError_t err = threads == kLargeCta ? cudaLaunchKernelEx(&cfg, topk_localize_kernel<kLargeCta>, p)
+                                               : cudaLaunchKernelEx(&cfg, topk_localize_kernel<kSmallCta>, p);
   if (err != cudaSuccess) {
     (void)cudaGetLastError();
     return -static_cast<int>(err);
@@ -803,8 +861,21 @@ extern "C" int silkern_topk_localize_v1(const float* logits, int64_t logits_stri
                                         int32_t* status, void* stream) {
   return silkern::topk_launch(logits, logits_stride, logits_width, seq_lens, req_ids, block_table, table_rows,
                               table_width, positions, out, counts, batch, top_k, block_size, dcp_size, dcp_rank,
-                              dcp_interleave, compact_valid_to_front, 0, -1, status,
+                              dcp_interleave, compact_valid_to_front, 0, -1, 0, status,
                               static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int silkern_topk_localize_explicit_v2(
+    const float* logits, int64_t logits_stride, int64_t logits_width, const int32_t* seq_lens,
+    const int32_t* req_ids, const int32_t* block_table, int64_t table_rows, int64_t table_width,
+    int32_t* positions, int32_t* out, int32_t* counts, int64_t batch, int32_t top_k, int32_t block_size,
+    int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave, int32_t compact_valid_to_front,
+    int32_t candidate_capacity, int32_t stage_table, int32_t cta_threads, int32_t* status, void* stream) {
+  if (candidate_capacity < 0 || stage_table < -1 || cta_threads < 0) return SILKERN_E_GEOMETRY;
+  return silkern::topk_launch(logits, logits_stride, logits_width, seq_lens, req_ids, block_table, table_rows,
+                              table_width, positions, out, counts, batch, top_k, block_size, dcp_size, dcp_rank,
+                              dcp_interleave, compact_valid_to_front, candidate_capacity, stage_table, cta_threads,
+                              status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int silkern_topk_localize_explicit_v1(
@@ -813,9 +884,9 @@ extern "C" int silkern_topk_localize_explicit_v1(
     int32_t* positions, int32_t* out, int32_t* counts, int64_t batch, int32_t top_k, int32_t block_size,
     int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave, int32_t compact_valid_to_front,
     int32_t candidate_capacity, int32_t stage_table, int32_t* status, void* stream) {
-  if (candidate_capacity < 0 || stage_table < -1) return SILKERN_E_GEOMETRY;
-  return silkern::topk_launch(logits, logits_stride, logits_width, seq_lens, req_ids, block_table, table_rows,
-                              table_width, positions, out, counts, batch, top_k, block_size, dcp_size, dcp_rank,
-                              dcp_interleave, compact_valid_to_front, candidate_capacity, stage_table, status,
-                              static_cast<cudaStream_t>(stream));
+  return silkern_topk_localize_explicit_v2(logits, logits_stride, logits_width, seq_lens, req_ids, block_table,
+                                           table_rows, table_width, positions, out, counts, batch, top_k,
+                                           block_size, dcp_size, dcp_rank, dcp_interleave,
+                                           compact_valid_to_front, candidate_capacity, stage_table, 0, status,
+                                           stream);
 }

@@ -54,6 +54,7 @@ def topk_localize(
     status=None,
     candidate_capacity: int = 0,
     stage_table: int = -1,
+    cta_threads: int = 0,
 ) -> None:
     """Select the top ``out.shape[1]`` positions of every logits row and localize them.
 
@@ -62,9 +63,10 @@ def topk_localize(
     (batch,); ``block_table`` int32 (rows, table_width); ``out`` int32
     (batch, top_k); ``counts`` int32 (batch,); ``positions`` optional int32
     (batch, top_k). Outputs must not share storage with inputs or with each
-    other. ``candidate_capacity`` (0 = library choice) and ``stage_table``
-    (-1 = library choice, 0 or 1) pin internals for tests and tuning; a
-    capacity of ``top_k`` forces the whole-row selection path. Raises
+    other. ``candidate_capacity`` (0 = library choice), ``stage_table``
+    (-1 = library choice, 0 or 1) and ``cta_threads`` (0 = library choice,
+    512 or 1024) pin internals for tests and tuning; a capacity of ``top_k``
+    forces the whole-row selection path. Raises
     :class:`LocalizationError` before launch on any unsupported binding or
     geometry.
     """
@@ -114,6 +116,8 @@ def topk_localize(
         raise LocalizationError("candidate_capacity must be a non-negative integer")
     if not _is_int(stage_table) or stage_table not in (-1, 0, 1):
         raise LocalizationError("stage_table must be -1, 0 or 1")
+    if not _is_int(cta_threads) or cta_threads not in (0, 512, 1024):
+        raise LocalizationError("cta_threads must be 0, 512 or 1024")
     status_ptr = _check_status(torch, status, device)
 
     lib = _native.load()
@@ -139,9 +143,9 @@ def topk_localize(
     ]
     with _device_scope(torch, device):
         stream = torch.cuda.current_stream(device).cuda_stream
-        if candidate_capacity or stage_table != -1:
-            code = lib.silkern_topk_localize_explicit_v1(
-                *args, int(candidate_capacity), int(stage_table), status_ptr, stream)
+        if candidate_capacity or stage_table != -1 or cta_threads:
+            code = lib.silkern_topk_localize_explicit_v2(
+                *args, int(candidate_capacity), int(stage_table), int(cta_threads), status_ptr, stream)
         else:
             code = lib.silkern_topk_localize_v1(*args, status_ptr, stream)
     _native.check(code, "topk_localize")

@@ -142,11 +142,12 @@ def test_topk_fuzz(seed) -> None:
         out = torch.empty((batch, top_k), dtype=torch.int32, device=DEV)
         counts = torch.empty(batch, dtype=torch.int32, device=DEV)
         pos = torch.empty((batch, top_k), dtype=torch.int32, device=DEV)
+        threads = int(rng.choice([0, 512, 1024]))
         topk_localize(torch.as_tensor(logits).to(DEV), torch.as_tensor(lens).to(DEV), torch.as_tensor(req).to(DEV),
-                      torch.as_tensor(table).to(DEV), out, counts, positions=pos, **geometry)
+                      torch.as_tensor(table).to(DEV), out, counts, positions=pos, cta_threads=threads, **geometry)
         torch.cuda.synchronize()
         want_pos, want_out, want_counts = oracle_topk(logits, lens, req, table, top_k=top_k, threads=4, **geometry)
-        ctx = (seed, trial, batch, width, top_k, kind, geometry)
+        ctx = (seed, trial, batch, width, top_k, kind, geometry, threads)
         assert np.array_equal(pos.cpu().numpy(), want_pos), ctx
         assert np.array_equal(out.cpu().numpy(), want_out), ctx
         assert np.array_equal(counts.cpu().numpy(), want_counts), ctx

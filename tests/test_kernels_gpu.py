@@ -229,6 +229,31 @@ def test_wide_table_is_gathered() -> None:
     assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
 
 
+@pytest.mark.parametrize(("bs", "dcp", "rank", "il"), [(64, 4, 3, 1), (48, 3, 1, 3), (1000, 1, 0, 1)])
+@pytest.mark.parametrize("cluster", [1, 4])
+def test_physical_slots_wrap_like_int32_lanes(bs, dcp, rank, il, cluster) -> None:
+    """Table entries over the whole int32 range: block * block_size + offset
+    overflows, and every entry point wraps it mod 2**32 as the reference's
+    int32 lanes do, bit for bit with the oracle."""
+    rng = np.random.default_rng(bs + 7 * dcp + cluster)
+    batch, width, table_width = 5, 4096, 64
+    tokens = rng.integers(-2, bs * table_width * dcp + bs, size=(batch, width), dtype=np.int32)
+    table = rng.integers(-(2**31), 2**31, size=(batch, table_width), dtype=np.int64).astype(np.int32)
+    table[0, :4] = [2**31 - 1, -(2**31), 2**25, -1]
+    req = rng.permutation(batch).astype(np.int32)
+    kw = dict(block_size=bs, dcp_size=dcp, dcp_rank=rank, dcp_interleave=il)
+    want = _oracle(req, table, tokens, **kw)
+    products = table.astype(np.int64) * bs
+    assert (products > 2**31 - 1).any() and (products < -(2**31)).any()  # the case overflows
+    for stage in (0, 1):
+        out, counts, _ = _explicit(req, table, tokens, cluster=cluster, stage=stage, prefetch=1, **kw)
+        assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1]), stage
+    out, counts = run_rowwise(req, table, tokens, **kw)
+    assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
+    out, counts = run_hierarchical(req, table, tokens, **kw)
+    assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
+
+
 @pytest.mark.parametrize("shift", [(0, 1, 2), (1, 3, 0), (3, 2, 1), (2, 0, 3)])
 @pytest.mark.parametrize("width", [7, 2048, 4096])
 def test_misaligned_views(shift, width) -> None:

@@ -29,7 +29,7 @@ def lib():
 
 def declared_symbols() -> set[str]:
     text = open(HEADER).read()
-    return set(re.findall(r"\b(silkern_\w+_v1)\s*\(", text))
+    return set(re.findall(r"\b(silkern_\w+_v\d+)\s*\(", text))
 
 
 def test_every_declared_symbol_is_exported(lib) -> None:
@@ -167,6 +167,8 @@ def topk(lib, explicit=None, **over):
     args = [a["logits"], a["stride"], a["width"], a["lens"], a["req"], a["table"], a["rows"], a["twidth"],
             a["pos"], a["out"], a["cnt"], a["batch"], a["k"], a["bs"], a["dcp"], a["rank"], a["il"],
             a["compact"]]
+    if explicit is not None and len(explicit) == 3:
+        return lib.silkern_topk_localize_explicit_v2(*args, *explicit, None, None)
     if explicit is not None:
         return lib.silkern_topk_localize_explicit_v1(*args, explicit[0], explicit[1], None, None)
     return lib.silkern_topk_localize_v1(*args, None, None)
@@ -204,6 +206,9 @@ def test_topk_explicit_rejects_bad_geometry(lib) -> None:
     assert topk(lib, explicit=(0, 2)) == 7  # stage_table not -1, 0 or 1
     assert topk(lib, explicit=(0, -2)) == 7
     assert topk(lib, explicit=(0, 1), twidth=4097, rows=1) == 7  # too wide to stage
+    assert topk(lib, explicit=(63, -1, 0)) == 7  # the same checks through v2
+    for threads in (-1, 1, 256, 513, 2048):  # CTA shape not 0, 512 or 1024
+        assert topk(lib, explicit=(0, -1, threads)) == 7
 
 
 def test_missing_library_fails_loudly(tmp_path) -> None:

@@ -100,10 +100,12 @@ def test_matches_oracle(shape, kind) -> None:
     assert np.array_equal(counts, want_counts)
 
 
+@pytest.mark.parametrize("threads", [512, 1024])
 @pytest.mark.parametrize("kind", ["normal", "ties"])
 @pytest.mark.parametrize(("capacity", "stage"), [(0, 0), (0, 1), (1000, -1), (1500, 1), (20000, 0)])
-def test_internal_paths(capacity, stage, kind) -> None:
-    """Both selection paths (a capacity of top_k forces the whole-row path) and both table sources."""
+def test_internal_paths(capacity, stage, kind, threads) -> None:
+    """Both selection paths (a capacity of top_k forces the whole-row path),
+    both table sources and both CTA shapes."""
     width, top_k, batch = 20000, 1000, 5
     rng = np.random.default_rng(7300 + capacity + stage + len(kind))
     logits = _values(rng, kind, (batch, width))
@@ -112,8 +114,25 @@ def test_internal_paths(capacity, stage, kind) -> None:
     req = np.arange(batch, dtype=np.int32)
     kw = dict(block_size=64, dcp_size=2, dcp_rank=0)
     pos, out, counts = _run(_dev(logits), lens, req, table, top_k, candidate_capacity=capacity,
-                            stage_table=stage, **kw)
+                            stage_table=stage, cta_threads=threads, **kw)
     want = oracle_topk(logits, lens, req, table, top_k=top_k, **kw)
+    assert np.array_equal(pos, want[0]) and np.array_equal(out, want[1]) and np.array_equal(counts, want[2])
+
+
+@pytest.mark.parametrize("kind", KINDS)
+@pytest.mark.parametrize("shape", SHAPES[1:6], ids=lambda s: "x".join(map(str, s)))
+def test_small_cta_shape_matches_oracle(shape, kind) -> None:
+    """Batches this small launch 1024-thread CTAs; the 512-thread shape of
+    larger batches, pinned, gives the same rows."""
+    batch, width, top_k = shape
+    rng = np.random.default_rng(7400 + 10 * SHAPES.index(shape) + KINDS.index(kind))
+    logits = _values(rng, kind, (batch, width))
+    lens = _lens(rng, batch, width, top_k)
+    table = _table(rng, 9, 1 + width // 64)
+    req = rng.integers(0, 9, size=batch).astype(np.int32)
+    geometry = GEOMETRIES[(SHAPES.index(shape) + len(kind) + 1) % len(GEOMETRIES)]
+    pos, out, counts = _run(_dev(logits), lens, req, table, top_k, cta_threads=512, **geometry)
+    want = oracle_topk(logits, lens, req, table, top_k=top_k, threads=8, **geometry)
     assert np.array_equal(pos, want[0]) and np.array_equal(out, want[1]) and np.array_equal(counts, want[2])
 
 
@@ -155,7 +174,25 @@ def test_threshold_bin_taken_whole(last_pass, capacity) -> None:
     table = _table(rng, batch, 400)
     req = np.arange(batch, dtype=np.int32)
     kw = dict(block_size=64, dcp_size=2, dcp_rank=1)
-    pos, out, counts = _run(_dev(logits), lens, req, table, top_k, candidate_capacity=capacity, **kw)
+    pos, out, counts = _run(_dev(logits), lens, req, table, top_k, candidate_capacity=capacity,
+                            cta_threads=512 if last_pass == 1 else 0, **kw)
+    want = oracle_topk(logits, lens, req, table, top_k=top_k, **kw)
+    assert np.array_equal(pos, want[0]) and np.array_equal(out, want[1]) and np.array_equal(counts, want[2])
+
+
+@pytest.mark.parametrize("stage", [0, 1])
+def test_physical_slots_wrap_like_int32_lanes(stage) -> None:
+    """Table entries over the whole int32 range: the slot arithmetic overflows
+    and wraps mod 2**32, as in the converter and the reference's int32 lanes."""
+    batch, width, top_k = 4, 30000, 2048
+    rng = np.random.default_rng(7340 + stage)
+    logits = rng.standard_normal((batch, width)).astype(np.float32)
+    lens = np.array([width, 20000, 2048, 2500], dtype=np.int32)
+    table = rng.integers(-(2**31), 2**31, size=(batch, 200), dtype=np.int64).astype(np.int32)
+    req = np.array([3, 1, 0, 2], dtype=np.int32)
+    kw = dict(block_size=48, dcp_size=3, dcp_rank=2, dcp_interleave=3)
+    assert (table.astype(np.int64) * 48 > 2**31 - 1).any()  # the case overflows
+    pos, out, counts = _run(_dev(logits), lens, req, table, top_k, stage_table=stage, **kw)
     want = oracle_topk(logits, lens, req, table, top_k=top_k, **kw)
     assert np.array_equal(pos, want[0]) and np.array_equal(out, want[1]) and np.array_equal(counts, want[2])
 
