@@ -690,10 +690,11 @@ def run_link(args, rank: int, world: int) -> dict | None:
 
     Per step, the end-to-end arm moves the workload's inputs to the device
     (one H2D copy per call: req_ids, table and tokens) and its results back
-    (two D2H copies per call: out and counts) from pinned host buffers. This
-    arm times those same copies with no kernel: H2D alone, D2H alone, and both
-    directions at once on two streams, which bounds the end-to-end step from
-    below. A comparison arm, rank 0 only; no localization runs.
+    (two D2H copies per call: out and counts) from pinned host buffers, the
+    steps alternating over ``--e2e-lanes`` streams. This arm times the same
+    copies on the same lanes with no kernel: H2D alone, D2H alone, and both
+    (the end-to-end step without its kernel). A comparison arm, rank 0 only;
+    no localization runs.
     """
     if rank != 0:
         return None
@@ -705,48 +706,46 @@ def run_link(args, rank: int, world: int) -> dict | None:
     case = _case(args.config, seed=0, dcp_rank=0)
     n_in = case.req_ids.size + case.block_table.size + case.tokens.size
     n_out = case.tokens.size
-    pairs = []
-    for _ in range(2 * calls):  # two buffer sets per call, alternating
-        pairs.append((torch.empty(n_in, dtype=torch.int32).pin_memory(),
-                      torch.empty(n_in, dtype=torch.int32, device=dev),
-                      torch.empty(n_out, dtype=torch.int32, device=dev),
-                      torch.empty(n_out, dtype=torch.int32).pin_memory(),
-                      torch.empty(case.batch, dtype=torch.int32, device=dev),
-                      torch.empty(case.batch, dtype=torch.int32).pin_memory()))
-    streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
+    n_lanes = max(1, args.e2e_lanes)
+    lanes = []  # per lane: its stream and one buffer set per call, as in the end-to-end arm
+    for _ in range(n_lanes):
+        sets = []
+        for _ in range(calls):
+            sets.append((torch.empty(n_in, dtype=torch.int32).pin_memory(),
+                         torch.empty(n_in, dtype=torch.int32, device=dev),
+                         torch.empty(n_out, dtype=torch.int32, device=dev),
+                         torch.empty(n_out, dtype=torch.int32).pin_memory(),
+                         torch.empty(case.batch, dtype=torch.int32, device=dev),
+                         torch.empty(case.batch, dtype=torch.int32).pin_memory()))
+        lanes.append((torch.cuda.Stream(device=dev), sets))
     steps = max(1, min(args.steps, 200))
 
-    def h2d(stream, step):
+    def step(i: int, inbound: bool, outbound: bool) -> None:
+        stream, sets = lanes[i % n_lanes]
         with torch.cuda.stream(stream):
-            for c in range(calls):
-                host_in, dev_in = pairs[(step % 2) * calls + c][:2]
-                dev_in.copy_(host_in, non_blocking=True)
+            for host_in, dev_in, dev_out, host_out, dev_counts, host_counts in sets:
+                if inbound:
+                    dev_in.copy_(host_in, non_blocking=True)
+                if outbound:
+                    host_out.copy_(dev_out, non_blocking=True)
+                    host_counts.copy_(dev_counts, non_blocking=True)
 
-    def d2h(stream, step):
-        with torch.cuda.stream(stream):
-            for c in range(calls):
-                _, _, dev_out, host_out, dev_counts, host_counts = pairs[(step % 2) * calls + c]
-                host_out.copy_(dev_out, non_blocking=True)
-                host_counts.copy_(dev_counts, non_blocking=True)
-
-    def timed(directions) -> float:
+    def timed(inbound: bool, outbound: bool) -> float:
         """Seconds per step, the best of three runs after a warm-up."""
         current = torch.cuda.current_stream(dev)
-        for step in range(max(3, args.warmup)):
-            for fn, stream in zip(directions, streams):
-                fn(stream, step)
+        for i in range(max(3, args.warmup)):
+            step(i, inbound, outbound)
         torch.cuda.synchronize(dev)
         best = math.inf
         for _ in range(3):
             start = torch.cuda.Event(enable_timing=True)
             end = torch.cuda.Event(enable_timing=True)
             start.record(current)
-            for stream in streams:
+            for stream, _ in lanes:
                 stream.wait_event(start)
-            for step in range(steps):
-                for fn, stream in zip(directions, streams):
-                    fn(stream, step)
-            for stream in streams:
+            for i in range(steps):
+                step(i, inbound, outbound)
+            for stream, _ in lanes:
                 current.wait_stream(stream)
             end.record(current)
             torch.cuda.synchronize(dev)
@@ -755,9 +754,9 @@ def run_link(args, rank: int, world: int) -> dict | None:
 
     h2d_bytes = 4 * n_in * calls
     d2h_bytes = 4 * (n_out + case.batch) * calls
-    t_in = timed([h2d])
-    t_out = timed([d2h])
-    t_both = timed([h2d, d2h])
+    t_in = timed(True, False)
+    t_out = timed(False, True)
+    t_both = timed(True, True)
     return {
         "impl": "host-link",
         "metric": "us per step, the end-to-end step's host copies alone (no kernel)",
@@ -773,7 +772,8 @@ def run_link(args, rank: int, world: int) -> dict | None:
         "h2d_gbs": h2d_bytes / t_in / 1e9,
         "d2h_gbs": d2h_bytes / t_out / 1e9,
         "both_gbs": (h2d_bytes + d2h_bytes) / t_both / 1e9,
-        "config": {"workload": WORKLOADS[args.config]["desc"], "buffers": "pinned host, two sets alternating"},
+        "config": {"workload": WORKLOADS[args.config]["desc"],
+                   "buffers": f"pinned host, {n_lanes} streams alternating, each with its own buffers"},
         "data": "synthetic",
     }
 
@@ -956,7 +956,8 @@ def run_e2e(args, cases, dev, dist) -> dict:
     arm = WORKLOADS[args.config]["arm"]
     lanes = []
     h2d = d2h = 0
-    for lane_index in range(2):
+    n_lanes = max(1, args.e2e_lanes)
+    for lane_index in range(n_lanes):
         stream = torch.cuda.Stream(device=dev)
         jobs = []
         for case in cases:
@@ -997,7 +998,7 @@ def run_e2e(args, cases, dev, dist) -> dict:
         lanes.append((stream, jobs))
 
     def step(i: int) -> None:
-        stream, jobs = lanes[i % 2]
+        stream, jobs = lanes[i % n_lanes]
         with torch.cuda.stream(stream):
             for host_in, dev_in, bufs, host_out, host_counts, call in jobs:
                 dev_in.copy_(host_in, non_blocking=True)
@@ -1049,9 +1050,9 @@ def run_e2e(args, cases, dev, dist) -> dict:
     torch.cuda.synchronize(dev)
 
     def replay(i: int) -> None:
-        stream, _ = lanes[i % 2]
+        stream, _ = lanes[i % n_lanes]
         with torch.cuda.stream(stream):
-            graphs[i % 2].replay()
+            graphs[i % n_lanes].replay()
 
     captured = timed(replay)
     del graphs
@@ -1065,7 +1066,7 @@ def run_e2e(args, cases, dev, dist) -> dict:
         "steps": steps,
         "us_per_step": captured * 1e6,
         "path": "silkern_b200 public launchers with host copies in and out every step, captured per "
-                "stream (CUDA graph) and replayed on 2 alternating streams, pinned host buffers",
+                f"stream (CUDA graph) and replayed on {n_lanes} alternating streams, pinned host buffers",
         "eager_us_per_step": eager * 1e6,
         "eager_value": world * indices / eager / 1e9,
     }
@@ -1082,6 +1083,8 @@ def main(argv=None) -> int:
     parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--batch", type=int, default=0, help="rows of the fused arm (default 256)")
+    parser.add_argument("--e2e-lanes", type=int, default=4,
+                        help="streams the end-to-end steps alternate over, each with its own buffers")
     args = parser.parse_args(argv)
     if args.steps < 1 or args.warmup < 0:
         parser.error("--steps must be >= 1 and --warmup >= 0")
