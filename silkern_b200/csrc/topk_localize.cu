@@ -5,13 +5,16 @@
 // those global positions into this DCP rank's physical KV slots. Run as two
 // kernels, the (batch, top_k) selection goes to HBM and comes back and the
 // second kernel pays a dependent-launch handoff. Here both are one kernel,
-// one CTA per row, every row of the batch resident at once:
+// one CTA per row, every row of the batch resident at once (1024-thread CTAs,
+// one per SM, when the batch fits the SMs; 512-thread CTAs, two per SM,
+// otherwise):
 //
 //   0. as soon as the row's length is known, bulk L2 prefetches
 //      (cp.async.bulk.prefetch.L2) start the whole row streaming from HBM;
 //   1. estimate: a histogram of the top 11 bits of the order key over every
 //      16th float4 of the row picks a floor bin that should leave ~1.5 x
-//      top_k scores at or above it;
+//      top_k scores at or above it (rows too short for the sample to reach a
+//      floor list every column);
 //   2. stream: the row is read once (128-bit loads, several 128-column blocks
 //      in flight per warp) and only a bit mask of the candidates (scores at or
 //      above the floor) is kept, per 128-column block;
@@ -22,7 +25,8 @@
 //      histogram;
 //   4. select: the three-pass radix select (11, 11 and 10 key bits) over the
 //      list finds the exact threshold key and how many keys equal to it are
-//      taken (the lowest positions);
+//      taken (the lowest positions); it ends at the first pass whose
+//      threshold bin is taken whole;
 //   5. emit: the selected positions, in ascending order, are the selection
 //      row; the converter's contract (silkern/contract.py:67-158: ownership,
 //      deinterleave, paged translation, stable compaction, counts) is applied
@@ -354,7 +358,8 @@ __global__ void __launch_bounds__(T, T == kSmallCta ? 2 : 1) topk_localize_kerne
   // included); a row with fewer than `want_sample` of them has no floor to
   // find, and lists every column.
   const uint32_t want_sample = static_cast<uint32_t>(k / kSampleEvery + k / (2 * kSampleEvery) + 16);
-  const bool sampled = len > k && 4u * static_cast<uint32_t>((len + 4 * kSampleEvery - 1) / (4 * kSampleEvery)) >= want_sample;
+  const uint32_t sample_values = 4u * static_cast<uint32_t>((len + 4 * kSampleEvery - 1) / (4 * kSampleEvery));
+  const bool sampled = len > k && sample_values >= want_sample;
   float4 first[2];
   if (sampled) {
     if (4 * g0 < len) first[0] = sample(g0);
