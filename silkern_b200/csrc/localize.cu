@@ -621,7 +621,9 @@ void smem_limits(int* per_sm, int* reserved) {
   }
   if (cache_sm[dev] == 0) {
     int a = 0, b = 0;
-    if (cudaDeviceGetAttribute(&a, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess || a <= 0) a = 233472;
+    if (cudaDeviceGetAttribute(&a, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess || a <= 0) {
+      a = 233472;
+    }
     if (cudaDeviceGetAttribute(&b, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess || b < 0) b = 1024;
     (void)cudaGetLastError();
     cache_res[dev] = b;

@@ -296,7 +296,8 @@ __device__ __forceinline__ void list_positions(const uint4* s_mask, int nb, int 
 }
 
 template <int T>
-__global__ void __launch_bounds__(T, T == kSmallCta ? 2 : 1) topk_localize_kernel(const __grid_constant__ TopkParams p) {
+__global__ void __launch_bounds__(T, T == kSmallCta ? 2 : 1)
+    topk_localize_kernel(const __grid_constant__ TopkParams p) {
   constexpr int kTopkThreads = T;
   constexpr int kTopkWarps = T / 32;
   extern __shared__ __align__(16) unsigned char smem[];
