@@ -42,3 +42,32 @@ def test_buffers_on_a_non_current_device(device_index) -> None:
     for got_out, got_counts in ((out, counts), (out_h, counts_h)):
         assert np.array_equal(got_out.cpu().numpy(), want[0])
         assert np.array_equal(got_counts.cpu().numpy(), want[1])
+
+
+@pytest.mark.parametrize("device_index", [1, 0])
+def test_fused_topk_on_a_non_current_device(device_index) -> None:
+    """The fused launcher's per-device state (SM count, shared-memory opt-in)
+    follows the buffers' device; both CTA shapes run there."""
+    from oracle.topk import topk_localize as oracle_topk
+    from silkern_b200 import topk_localize
+
+    rng = np.random.default_rng(31 + device_index)
+    dev = torch.device("cuda", device_index)
+    other = 1 - device_index
+    batch, width, top_k = 6, 20000, 1024
+    logits = rng.standard_normal((batch, width)).astype(np.float32)
+    lens = rng.integers(0, width + 1, size=batch).astype(np.int32)
+    table = rng.integers(-5, 1 << 20, size=(4, 400)).astype(np.int32)
+    req = rng.integers(0, 4, size=batch).astype(np.int32)
+    kw = dict(block_size=32, dcp_size=2, dcp_rank=1)
+    want = oracle_topk(logits, lens, req, table, top_k=top_k, **kw)
+    for threads in (0, 512):
+        out = torch.empty((batch, top_k), dtype=torch.int32, device=dev)
+        counts = torch.empty(batch, dtype=torch.int32, device=dev)
+        with torch.cuda.device(other):
+            topk_localize(torch.as_tensor(logits).to(dev), torch.as_tensor(lens).to(dev),
+                          torch.as_tensor(req).to(dev), torch.as_tensor(table).to(dev), out, counts,
+                          cta_threads=threads, **kw)
+        torch.cuda.synchronize(dev)
+        assert np.array_equal(out.cpu().numpy(), want[1]), threads
+        assert np.array_equal(counts.cpu().numpy(), want[2]), threads
