@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
                     [--impl ours|reference|triton|vllm|fused|atomic|link] [--config C] [--batch B]
+                    [--rows R] [--e2e-steps S] [--e2e-lanes L] [--no-cpu-baseline]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
 
 Default workload (config 3, one step = one converter call): a selection batch
@@ -812,9 +813,13 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     plan = shard_plan(rank, world, config)
 
     distinct = calls if calls > 1 else DISTINCT_CASES
+    if args.rows > 0:  # fewer, larger cases: every call's rows repeat a config case's
+        distinct = calls if calls > 1 else 2
     cases = [_case(config, seed=plan["base_seed"] + i, dcp_rank=plan["dcp_rank"]) for i in range(distinct)]
+    if args.rows > 0:
+        cases = [_stack_rows(c, args.rows) for c in cases]
     bytes_per_call = cases[0].algorithmic_bytes()
-    n_sets = max(64, math.ceil(2.05 * L2_BYTES / bytes_per_call))
+    n_sets = max(64 if args.rows == 0 else 2, math.ceil(2.05 * L2_BYTES / bytes_per_call))
     n_sets = math.ceil(n_sets / distinct) * distinct
     sets = []
     for i in range(n_sets):
@@ -905,7 +910,11 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
 
     peaks = _peaks()
     achieved = bytes_per_call / per_call_s / 1e9
-    traffic = _traffic(config)
+    traffic = _traffic(config) if args.rows == 0 else None  # the committed capture is of the default rows
+    workload = _workload_config(config, world, n_sets)
+    if args.rows > 0:
+        workload["rows_per_call"] = args.rows
+        workload["workload"] += f"; {args.rows} rows per call, the config's rows repeated"
     result = {
         **({"impl": "atomic-baseline"} if args.impl == "atomic" else {}),
         "metric": METRIC if config == 3 else f"Gindices/s per B200, config {config}",
@@ -921,7 +930,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
         "vs_baseline": None,
         "dtype": "int32",
         "data": f"synthetic (seeded; config {config} shapes)",
-        "config": _workload_config(config, world, n_sets),
+        "config": workload,
         "bit_exact": bit_exact,
         "hbm_gbs": achieved,
         "roofline": {
@@ -944,6 +953,18 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = _cpu_baseline(config, _host_threads())
     return result if rank == 0 else None
+
+
+def _stack_rows(case, rows: int):
+    """`case` with `rows` selection rows: its own rows repeated in order (the
+    requests and the block table unchanged)."""
+    import dataclasses
+
+    import numpy as np
+
+    reps = -(-rows // case.batch)
+    return dataclasses.replace(case, req_ids=np.ascontiguousarray(np.tile(case.req_ids, reps)[:rows]),
+                               tokens=np.ascontiguousarray(np.tile(case.tokens, (reps, 1))[:rows]))
 
 
 def run_e2e(args, cases, dev, dist) -> dict:
@@ -1083,6 +1104,8 @@ def main(argv=None) -> int:
     parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--batch", type=int, default=0, help="rows of the fused arm (default 256)")
+    parser.add_argument("--rows", type=int, default=0,
+                        help="rows per converter call: the workload's rows repeated (default: its own batch)")
     parser.add_argument("--e2e-lanes", type=int, default=4,
                         help="streams the end-to-end steps alternate over, each with its own buffers")
     args = parser.parse_args(argv)
