@@ -22,11 +22,12 @@
 //      gives each warp its base; across a cluster, each CTA pushes its total
 //      into every CTA's shared memory (DSMEM) before one cluster barrier.
 //      No atomics, so the order is the selector's order on every run;
-//   4. survivors are staged in shared memory at their final positions, then
-//      each thread writes its output granules once with 128-bit stores
-//      (survivors, then -1); across a cluster, a CTA's survivors are one
-//      contiguous run, copied out 128-bit wide, plus the -1 tail of its own
-//      slice. Every output element is written exactly once.
+//   4. without a cluster, each survivor is stored straight to its final
+//      position and the granules past the row's count are filled with -1
+//      (128-bit stores); across a cluster, a CTA's survivors are staged in
+//      shared memory and copied out 128-bit wide as one contiguous run, plus
+//      the -1 tail of its own slice. Every output element is written exactly
+//      once.
 //
 // Semantics follow silkern/contract.py:67-158 (localize_reference) and the
 // int32 lanes of silkern/kernels.py:51-125 (_rowwise_kernel).
@@ -276,9 +277,9 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
       uint32_t lb, local;
       const bool ok = map_token(val[i][j], &lb, &local);
       if constexpr (!STAGE) {
-        int32_t phys = COMPACT ? 0 : -1;
-        if (ok) phys = physical(__ldg(trow + lb), lb, local);
-        val[i][j] = phys;
+        // branch-free: an invalid token reads entry 0 of the row, unused
+        const int32_t blk = __ldg(trow + (ok ? lb : 0u));
+        val[i][j] = ok ? physical(blk, lb, local) : (COMPACT ? 0 : -1);
       }
       b |= ok ? (1u << j) : 0u;
     }
@@ -362,50 +363,54 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
 
   int32_t* orow = p.out + row * p.width;
   if constexpr (COMPACT) {
-    // Stage this CTA's survivors compactly in shared memory, then write them
-    // and the -1 tail with 128-bit stores, each output element once.
-    int32_t* s_row = gsmem + p.smem_row;
+    if constexpr (!CLUSTER) {
+      // The whole row is this CTA's: each survivor goes straight to its final
+      // position, and the granules at or past cta_total are filled with -1.
+      // Every output element is written once.
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      int32_t* dst = s_row + base[i] + lane_pre[i];
-      int k = 0;
+      for (int i = 0; i < NC; ++i) {
+        int32_t* dst = orow + base[i] + lane_pre[i];
+        int k = 0;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (bits[i] & (1u << j)) dst[k] = val[i][j];
-        k += (bits[i] >> j) & 1u;
+        for (int j = 0; j < 4; ++j) {
+          if (bits[i] & (1u << j)) dst[k] = val[i][j];
+          k += (bits[i] >> j) & 1u;
+        }
       }
-    }
-    __syncthreads();
-    if constexpr (CLUSTER) {
-      copy_from_shared(orow + row_off, s_row, cta_total, tid, nthreads);
-      fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
-    } else {
-      // The whole row is this CTA's: granule g holds survivors below
-      // cta_total and -1 from there on.
+      if (tiles) __syncthreads();  // s_tile is complete
       const bool out_vec = (reinterpret_cast<uintptr_t>(orow) & 15u) == 0;
 #pragma unroll
       for (int i = 0; i < NC; ++i) {
         const int col = 4 * (i * nthreads + tid);
-        if (col < len) {
-          int4 v;
-          if (col + 4 <= cta_total) {
-            v = *reinterpret_cast<const int4*>(s_row + col);
-          } else if (col >= cta_total) {
-            v = make_int4(-1, -1, -1, -1);
+        if (col < len && col + 4 > cta_total) {  // this granule holds part of the -1 tail
+          if (out_vec && col >= cta_total && col + 4 <= len) {
+            *reinterpret_cast<int4*>(orow + col) = make_int4(-1, -1, -1, -1);
           } else {
-            const int4 q = *reinterpret_cast<const int4*>(s_row + col);
-            v = make_int4(q.x, col + 1 < cta_total ? q.y : -1, col + 2 < cta_total ? q.z : -1, -1);
-          }
-          if (out_vec && col + 4 <= len) {
-            *reinterpret_cast<int4*>(orow + col) = v;
-          } else {
-            orow[col] = v.x;
-            if (col + 1 < len) orow[col + 1] = v.y;
-            if (col + 2 < len) orow[col + 2] = v.z;
-            if (col + 3 < len) orow[col + 3] = v.w;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (col + j >= cta_total && col + j < len) orow[col + j] = -1;
+            }
           }
         }
       }
+    } else {
+      // Stage this CTA's survivors compactly in shared memory, then copy them
+      // out as one contiguous run at the row offset, plus the -1 tail of the
+      // CTA's own slice.
+      int32_t* s_row = gsmem + p.smem_row;
+#pragma unroll
+      for (int i = 0; i < NC; ++i) {
+        int32_t* dst = s_row + base[i] + lane_pre[i];
+        int k = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (bits[i] & (1u << j)) dst[k] = val[i][j];
+          k += (bits[i] >> j) & 1u;
+        }
+      }
+      __syncthreads();
+      copy_from_shared(orow + row_off, s_row, cta_total, tid, nthreads);
+      fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
     }
   } else {
     if (tiles) __syncthreads();  // the compacting path's staging barrier covers s_tile
