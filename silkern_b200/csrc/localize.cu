@@ -347,7 +347,7 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
 
   // Hierarchical: the CTA-local exclusive position of the element in each
   // tile's first column is that tile's offset (before the row offset), staged
-  // in shared memory ahead of the barrier that publishes the survivors.
+  // in shared memory ahead of a barrier that precedes the publishing loop.
   int32_t* s_tile = gsmem + p.smem_tile;
   const bool tiles = p.tile_shift >= 0;
   if (tiles) {
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
       fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
     }
   } else {
-    if (tiles) __syncthreads();  // the compacting path's staging barrier covers s_tile
+    if (tiles) __syncthreads();  // s_tile is complete
     int32_t* dst = orow + c0;
     const bool out_vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
 #pragma unroll
