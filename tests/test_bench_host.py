@@ -88,3 +88,53 @@ def test_reference_arm_other_ranks_print_nothing() -> None:
         capture_output=True, text=True, timeout=300, check=True, env=env,
     )
     assert proc.stdout.strip() == ""
+
+
+def test_stacked_rows_repeat_the_case_in_order() -> None:
+    """`--rows R`: a call of R rows is the config's rows repeated, with the
+    requests repeated alongside and the block table unchanged."""
+    import numpy as np
+
+    from silkern_b200.workloads import config_case
+
+    case = config_case(2, seed=3)
+    stacked = bench._stack_rows(case, 150)
+    assert stacked.tokens.shape == (150, case.width)
+    assert stacked.req_ids.shape == (150,)
+    assert np.array_equal(stacked.tokens[:64], case.tokens)
+    assert np.array_equal(stacked.tokens[64:128], case.tokens)
+    assert np.array_equal(stacked.tokens[128:], case.tokens[:22])
+    assert np.array_equal(stacked.req_ids[64:128], case.req_ids)
+    assert stacked.block_table is case.block_table
+    assert stacked.geometry() == case.geometry()
+    assert stacked.tokens.flags.c_contiguous and stacked.req_ids.flags.c_contiguous
+
+
+def test_cli_accepts_the_sizing_and_lane_options() -> None:
+    """The options that size the work parse, with the defaults the bench
+    documents (the run itself needs a GPU)."""
+    import argparse
+
+    seen = {}
+
+    def fake_parse(self, argv=None, namespace=None):
+        args = original(self, argv, namespace)
+        seen.update(vars(args))
+        raise SystemExit(0)
+
+    original = argparse.ArgumentParser.parse_args
+    argparse.ArgumentParser.parse_args = fake_parse
+    try:
+        with pytest.raises(SystemExit):
+            bench.main(["--impl", "link", "--rows", "4096", "--e2e-lanes", "8", "--batch", "16"])
+    finally:
+        argparse.ArgumentParser.parse_args = original
+    assert seen["impl"] == "link" and seen["rows"] == 4096 and seen["e2e_lanes"] == 8 and seen["batch"] == 16
+    seen.clear()
+    argparse.ArgumentParser.parse_args = fake_parse
+    try:
+        with pytest.raises(SystemExit):
+            bench.main([])
+    finally:
+        argparse.ArgumentParser.parse_args = original
+    assert seen["impl"] == "ours" and seen["rows"] == 0 and seen["e2e_lanes"] == 4 and seen["config"] == 3
