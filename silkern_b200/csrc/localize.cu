@@ -22,12 +22,11 @@
 //      gives each warp its base; across a cluster, each CTA pushes its total
 //      into every CTA's shared memory (DSMEM) before one cluster barrier.
 //      No atomics, so the order is the selector's order on every run;
-//   4. without a cluster, each survivor is stored straight to its final
-//      position and the granules past the row's count are filled with -1
-//      (128-bit stores); across a cluster, a CTA's survivors are staged in
-//      shared memory and copied out 128-bit wide as one contiguous run, plus
-//      the -1 tail of its own slice. Every output element is written exactly
-//      once.
+//   4. each survivor is stored straight to its final position (across a
+//      cluster, after the CTA's row offset); without a cluster the granules
+//      past the row's count are filled with -1, across a cluster each CTA
+//      fills the -1 tail of its own slice (128-bit stores on the aligned
+//      body). Every output element is written exactly once.
 //
 // Semantics follow silkern/contract.py:67-158 (localize_reference) and the
 // int32 lanes of silkern/kernels.py:51-125 (_rowwise_kernel).
@@ -73,7 +72,6 @@ struct Params {
   int32_t tile_shift;     // log2(tile_size) when publishing tiles, else -1
   int32_t tiles_per_row;
   int32_t smem_group;     // ints of dynamic shared memory per row group
-  int32_t smem_row;       // offset of the survivor stage in a group's region
   int32_t smem_wt;        // offset of the warp totals in a group's region
   int32_t smem_tile;      // offset of the tile offsets in a group's region
   int32_t row_threads;    // threads per row group (a power of two without a cluster)
@@ -106,24 +104,6 @@ __device__ __forceinline__ void fill_invalid(int32_t* row, int lo, int hi, int t
   if (tid < rest) dst[head + 4 * nvec + tid] = -1;
 }
 
-// dst[0:n] = src[0:n] (src in shared memory) with 128-bit stores on the
-// aligned body of dst.
-__device__ __forceinline__ void copy_from_shared(int32_t* dst, const int32_t* src, int n, int tid,
-                                                 int nthreads) {
-  if (n <= 0) return;
-  int head = static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 2);
-  head = head < n ? head : n;
-  if (tid < head) dst[tid] = src[tid];
-  const int nvec = (n - head) >> 2;
-  int4* body = reinterpret_cast<int4*>(dst + head);
-  const int32_t* s = src + head;
-  for (int g = tid; g < nvec; g += nthreads) {
-    body[g] = make_int4(s[4 * g], s[4 * g + 1], s[4 * g + 2], s[4 * g + 3]);
-  }
-  const int rest = n - head - 4 * nvec;
-  if (tid < rest) dst[head + 4 * nvec + tid] = src[head + 4 * nvec + tid];
-}
-
 // NC chunks of four columns per thread; CLUSTER: rows split over a cluster;
 // MODE: general arithmetic, all powers of two, or all powers of two with
 // interleave 1; STAGE: the block-table row is staged in shared memory instead
@@ -139,7 +119,7 @@ template <int NC, bool CLUSTER, int MODE, bool STAGE, bool COMPACT>
 __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxThreads,
                                   (NC == 1 && !CLUSTER) ? 2 : 1)
     localize_kernel(const __grid_constant__ Params p) {
-  extern __shared__ __align__(16) int32_t smem[];  // per row group: [table][survivors][warp totals][tiles]
+  extern __shared__ __align__(16) int32_t smem[];  // per row group: [table][warp totals][tiles]
   __shared__ int32_t s_cta_total[kMaxCluster];
 
   int nthreads, tid, group;
@@ -394,13 +374,12 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
         }
       }
     } else {
-      // Stage this CTA's survivors compactly in shared memory, then copy them
-      // out as one contiguous run at the row offset, plus the -1 tail of the
+      // Each survivor straight to its final position (this CTA's run starts at
+      // the row offset from the cluster exchange), then the -1 tail of the
       // CTA's own slice.
-      int32_t* s_row = gsmem + p.smem_row;
 #pragma unroll
       for (int i = 0; i < NC; ++i) {
-        int32_t* dst = s_row + base[i] + lane_pre[i];
+        int32_t* dst = orow + row_off + base[i] + lane_pre[i];
         int k = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -408,8 +387,7 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
           k += (bits[i] >> j) & 1u;
         }
       }
-      __syncthreads();
-      copy_from_shared(orow + row_off, s_row, cta_total, tid, nthreads);
+      if (tiles) __syncthreads();  // s_tile is complete
       fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
     }
   } else {
@@ -843,12 +821,10 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req, i
   KernelFn fn = pick_kernel(g.nc, g.cluster > 1, mode, g.stage, p.compact != 0);
   if (fn == nullptr) return SILKERN_E_GEOMETRY;
   const int ntiles_cta = r.tile_size ? (g.slice + r.tile_size - 1) / r.tile_size : 0;
-  // dynamic shared memory per row group: [table stage][survivor stage][warp
-  // totals][tile offsets], every part 16-byte aligned
+  // dynamic shared memory per row group: [table stage][warp totals][tile
+  // offsets], every part 16-byte aligned
   const int stage_ints = g.stage ? static_cast<int>((r.table_width + 3) / 4 * 4) : 0;
-  const int row_ints = p.compact ? (g.slice + 3) / 4 * 4 : 0;
-  p.smem_row = stage_ints;
-  p.smem_wt = stage_ints + row_ints;
+  p.smem_wt = stage_ints;
   p.smem_tile = p.smem_wt + g.nc * 32;
   p.smem_group = (p.smem_tile + ntiles_cta + 3) / 4 * 4;
   size_t smem = sizeof(int32_t) * static_cast<size_t>(p.smem_group) * static_cast<size_t>(g.rows_per_cta);
