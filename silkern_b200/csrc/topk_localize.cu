@@ -94,6 +94,8 @@ struct TopkParams {
   uint32_t dcp_rank, dcp_size, interleave;
   int32_t block_size;
   FastDiv div_il, div_dcp, div_bs;
+  int32_t pow2;  // interleave, dcp_size and block_size all powers of two: shifts below
+  uint32_t il_shift, dcp_shift, bs_shift;
   // dynamic shared memory layout (byte offsets, 16-byte aligned)
   int32_t off_boff, off_key, off_pos, off_table;
 };
@@ -115,6 +117,13 @@ __device__ __forceinline__ float key_floor(uint32_t key) {
 // (silkern/contract.py:132-149).
 __device__ __forceinline__ bool owned(const TopkParams& p, uint32_t u, uint32_t twidth, uint32_t* lb,
                                       uint32_t* local) {
+  if (p.pow2) {
+    const uint32_t q1 = u >> p.il_shift;
+    const uint32_t q2 = q1 >> p.dcp_shift;
+    *local = (q2 << p.il_shift) | (u & (p.interleave - 1u));
+    *lb = *local >> p.bs_shift;
+    return (q1 & (p.dcp_size - 1u)) == p.dcp_rank && *lb < twidth;
+  }
   const uint32_t q1 = fastdiv(u, p.div_il);   // u / interleave
   const uint32_t q2 = fastdiv(q1, p.div_dcp);  // u / (dcp_size * interleave)
   *local = q2 * p.interleave + (u - q1 * p.interleave);
@@ -835,6 +844,17 @@ int topk_launch(const float* logits, int64_t stride, int64_t width, const int32_
   p.div_il = make_fastdiv(p.interleave);
   p.div_dcp = make_fastdiv(p.dcp_size);
   p.div_bs = make_fastdiv(static_cast<uint32_t>(block_size));
+  auto pow2_shift = [](uint32_t v, uint32_t* shift) {
+    if ((v & (v - 1u)) != 0u) return false;
+    uint32_t s = 0;
+    while ((1u << s) < v) ++s;
+    *shift = s;
+    return true;
+  };
+  p.pow2 = (pow2_shift(p.interleave, &p.il_shift) && pow2_shift(p.dcp_size, &p.dcp_shift) &&
+            pow2_shift(static_cast<uint32_t>(block_size), &p.bs_shift))
+               ? 1
+               : 0;
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(batch), 1, 1);
