@@ -63,8 +63,9 @@ extern "C" {
 
 /*
  * Row-wise stable localization: one launch; each row is scanned by one CTA
- * (or, for long rows with few requests, by a thread-block cluster that
- * exchanges per-CTA counts through distributed shared memory).
+ * or by a group of threads inside one (or, for long rows with few requests,
+ * by a thread-block cluster that exchanges per-CTA counts through distributed
+ * shared memory).
  * Replaces silkern/kernels.py:318-434 (localize_rowwise and _rowwise_kernel,
  * kernels.py:51-125). block_table is (table_rows, table_width); tokens and
  * out are (batch, width); req_ids and counts are (batch,).
@@ -115,9 +116,9 @@ int silkern_workspace_shapes_v1(int64_t batch, int64_t width, int32_t tile_size,
  * stage_table = 1 stages the request's block-table row in shared memory
  * (table_width <= 4096), 0 gathers it from global memory, -1 lets the
  * library decide; prefetch_table likewise for the L2 bulk prefetch of the
- * whole table; chunks_per_thread (1, 2, 4 or 8; 0 = library choice) sets how
- * many four-column chunks each thread maps. tile_size = 0 selects row-wise
- * semantics (no workspace).
+ * whole table; chunks_per_thread (1, 2, 4 or 8; 0 = library choice) makes
+ * each thread map a run of 4 x chunks_per_thread consecutive columns.
+ * tile_size = 0 selects row-wise semantics (no workspace).
  * Same semantics and outputs as the entry points above. No counterpart in the
  * reference (its launch geometry is fixed inside each launcher).
  */

@@ -1,9 +1,11 @@
 // Sparse-index localization for decode context parallelism on B200 (sm_100a).
 //
-// One kernel serves both public entry points. A row of `width` selected token
-// positions is split into `cluster` contiguous column slices; each slice is
-// one CTA, and the CTAs of one row form a thread-block cluster (cluster == 1
-// for the common row-wise case). Per CTA:
+// One kernel family serves both public entry points. A row of `width`
+// selected token positions is split into `cluster` contiguous column slices;
+// each slice is one CTA, and the CTAs of one row form a thread-block cluster
+// (cluster == 1 for the common row-wise case, where several rows can share a
+// CTA as independent row groups). Each thread owns a run of G consecutive
+// columns of its slice (G = 4, 8, 16 or 32). Per CTA:
 //
 //   0. before waiting on the previous grid (programmatic dependent launch),
 //      ask L2 for this slice's tokens, the row's request id and this CTA's
@@ -11,22 +13,27 @@
 //      device's point of coherence, so it never returns stale data: loads
 //      issued after the wait see every write of the previous grid. Call
 //      N + 1 therefore reads DRAM while call N is still running;
-//   1. read the request id and the slice's tokens (128-bit loads when the
-//      slice start is 16-byte aligned);
-//   2. apply ownership, deinterleave and paged translation with shifts (all
-//      powers of two) or invariant-divisor multiplies (general case), and
-//      gather the physical block of each valid element from the request's
-//      block-table row (L2-resident after step 0, or staged in shared memory);
-//   3. stable compaction: warp ballots give each lane its prefix inside the
-//      warp, warp totals go through shared memory and one redux.sync per chunk
-//      gives each warp its base; across a cluster, each CTA pushes its total
-//      into every CTA's shared memory (DSMEM) before one cluster barrier.
-//      No atomics, so the order is the selector's order on every run;
-//   4. each survivor is stored straight to its final position (across a
-//      cluster, after the CTA's row offset); without a cluster the granules
-//      past the row's count are filled with -1, across a cluster each CTA
-//      fills the -1 tail of its own slice (128-bit stores on the aligned
-//      body). Every output element is written exactly once.
+//   1. read the request id, the thread's run of tokens (one 256-bit load per
+//      eight columns when the run is 32-byte aligned) and, when the table is
+//      staged, the request's block-table row into shared memory in the same
+//      wave (speculating that row r belongs to request r, repaired when not);
+//   2. apply ownership and deinterleave: with interleave 1 and powers of two,
+//      one rotate and one unsigned compare decide ownership, sign and table
+//      bounds together; otherwise shifts or invariant-divisor multiplies;
+//   3. stable compaction: each thread counts its valid elements, ballots over
+//      the count's bits give each thread its exclusive prefix in the warp,
+//      warp totals go through shared memory and one redux.sync gives each
+//      warp its base; across a cluster, each CTA pushes its total into every
+//      CTA's shared memory (DSMEM) before one cluster barrier. No atomics, so
+//      the order is the selector's order on every run;
+//   4. paged translation: each valid element reads its block from the staged
+//      table row (or, unstaged, from the L2 gather issued in step 2);
+//   5. a row that is one CTA's is staged in shared memory at its final
+//      positions and written run by run, each thread storing its own
+//      columns (survivors, then -1 past the count) with 256-bit stores;
+//      across a cluster, each CTA stores its survivors after its row offset
+//      and fills the -1 tail of its own slice. Every output element is
+//      written exactly once.
 //
 // Semantics follow silkern/contract.py:67-158 (localize_reference) and the
 // int32 lanes of silkern/kernels.py:51-125 (_rowwise_kernel).
@@ -42,15 +49,15 @@
 
 namespace silkern {
 
-constexpr int kMaxThreads = 512;      // threads per row group
-constexpr int kMaxCtaThreads = 1024;  // threads per CTA (row groups of one-chunk rows)
-constexpr int kMaxRowGroups = 15;     // row groups per CTA: named barriers 1..15
+constexpr int kMaxThreads = 512;      // threads per CTA (row groups, or one cluster slice)
 constexpr int kMaxCluster = 8;
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
+constexpr int kStageSmemMax = 96 * 1024;  // shared memory per CTA for an automatic stage
+constexpr int kSmemMax = 200 * 1024;      // dynamic shared memory per CTA, any launch
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr int kModeGeneral = 0;  // invariant-divisor multiplies
 constexpr int kModePow2 = 1;     // interleave, dcp_size, block_size powers of two
-constexpr int kModePow2Il1 = 2;  // ... and interleave 1, single bounds compare
+constexpr int kModePow2Il1 = 2;  // ... and interleave 1: rotate + one compare
 
 struct Params {
   const int32_t* req_ids;
@@ -65,15 +72,16 @@ struct Params {
   uint64_t table_bytes;   // bytes of the block table covered by the L2 prefetch
   uint32_t table_chunk;   // per-CTA share of that prefetch (multiple of 16), 0 = off
   uint32_t table_width;
+  uint32_t local_limit;   // interleave-1 mode: a valid element's local position is below this
   int32_t width;
   int32_t slice;          // columns per CTA
   int32_t cluster;        // CTAs per row
-  int32_t compact;        // compaction on (selects the kernel instantiation)
   int32_t tile_shift;     // log2(tile_size) when publishing tiles, else -1
   int32_t tiles_per_row;
   int32_t smem_group;     // ints of dynamic shared memory per row group
-  int32_t smem_wt;        // offset of the warp totals in a group's region
-  int32_t smem_tile;      // offset of the tile offsets in a group's region
+  int32_t smem_out;       // offset of the staged output in a group's region
+  int32_t smem_wt;        // offset of the warp totals
+  int32_t smem_tile;      // offset of the tile offsets
   int32_t row_threads;    // threads per row group (a power of two without a cluster)
   int32_t row_threads_shift;
   int32_t rows_base;      // rows per CTA: rows_base, plus one for the first rows_extra CTAs
@@ -84,8 +92,8 @@ struct Params {
   uint32_t block_size;
   // general path
   FastDiv div_il, div_dcp, div_bs;
-  // all-powers-of-two path
-  uint32_t il_shift, group_shift, bs_shift, lb_shift;
+  // all-powers-of-two paths
+  uint32_t il_shift, dcp_shift, group_shift, bs_shift;
   uint32_t il_mask, dcp_mask, bs_mask;
 };
 
@@ -104,10 +112,77 @@ __device__ __forceinline__ void fill_invalid(int32_t* row, int lo, int hi, int t
   if (tid < rest) dst[head + 4 * nvec + tid] = -1;
 }
 
-// NC chunks of four columns per thread; CLUSTER: rows split over a cluster;
-// MODE: general arithmetic, all powers of two, or all powers of two with
-// interleave 1; STAGE: the block-table row is staged in shared memory instead
-// of gathered from L2; COMPACT: valid values go to the front of the row.
+// v[0..G) = src[0..n) and -1 past n (n may be <= 0): 256-bit loads when the
+// run is whole and 32-byte aligned, 128-bit when 16-byte aligned, else scalar.
+template <int G>
+__device__ __forceinline__ void load_run(const int32_t* src, int n, int32_t (&v)[G]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+  if (n >= G && (G % 8 == 0) && (a & 31u) == 0) {
+#pragma unroll
+    for (int i = 0; i < G / 8; ++i) {
+      int32_t q[8];
+      ld_nc_v8(src + 8 * i, q);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[8 * i + j] = q[j];
+    }
+  } else if (n >= G && (a & 15u) == 0) {
+#pragma unroll
+    for (int i = 0; i < G / 4; ++i) {
+      const int4 q = __ldg(reinterpret_cast<const int4*>(src) + i);
+      v[4 * i + 0] = q.x;
+      v[4 * i + 1] = q.y;
+      v[4 * i + 2] = q.z;
+      v[4 * i + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < G; ++j) v[j] = j < n ? __ldg(src + j) : -1;
+  }
+}
+
+// dst[0..min(n, G)) = w[0..): the widest aligned stores the run allows.
+template <int G>
+__device__ __forceinline__ void store_run(int32_t* dst, int n, const int32_t (&w)[G]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(dst);
+  if (n >= G && (G % 8 == 0) && (a & 31u) == 0) {
+#pragma unroll
+    for (int i = 0; i < G / 8; ++i) {
+      int32_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = w[8 * i + j];
+      st_v8(dst + 8 * i, q);
+    }
+  } else if (n >= G && (a & 15u) == 0) {
+#pragma unroll
+    for (int i = 0; i < G / 4; ++i) {
+      reinterpret_cast<int4*>(dst)[i] = make_int4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      if (j < n) dst[j] = w[j];
+    }
+  }
+}
+
+// Exclusive prefix of c over the lanes of the warp, from one ballot per bit
+// of c (c < 2^BITS).
+template <int BITS>
+__device__ __forceinline__ int warp_exclusive(uint32_t c) {
+  const uint32_t lt = lanemask_lt();
+  int e = 0;
+#pragma unroll
+  for (int b = 0; b < BITS; ++b) e += __popc(__ballot_sync(kFull, (c >> b) & 1u) & lt) << b;
+  return e;
+}
+
+__host__ __device__ constexpr int count_bits(int g) { return g < 2 ? 1 : 1 + count_bits(g >> 1); }
+
+// G columns per thread; CLUSTER: rows split over a cluster; MODE: general
+// arithmetic, all powers of two, or all powers of two with interleave 1;
+// COMPACT: valid values go to the front of the row; STAGE: the request's
+// block-table row is staged in shared memory and read only for valid
+// elements, instead of gathered from L2 for every element.
 //
 // Without a cluster a CTA holds p.rows_base or p.rows_base + 1 consecutive
 // rows, one group of p.row_threads threads per row (each group with its own
@@ -115,11 +190,11 @@ __device__ __forceinline__ void fill_invalid(int32_t* row, int lo, int hi, int t
 // the load even under programmatic dependent launch: the next call's CTAs
 // become resident where this call left room, and with one-row CTAs several of
 // them could pile onto one SM.
-template <int NC, bool CLUSTER, int MODE, bool STAGE, bool COMPACT>
-__global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxThreads,
-                                  (NC == 1 && !CLUSTER) ? 2 : 1)
+template <int G, bool CLUSTER, int MODE, bool COMPACT, bool STAGE>
+__global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 8) ? 1 : 2)
     localize_kernel(const __grid_constant__ Params p) {
-  extern __shared__ __align__(16) int32_t smem[];  // per row group: [table][warp totals][tiles]
+  // per row group: [staged table row][staged output][warp totals][tile offsets]
+  extern __shared__ __align__(16) int32_t smem[];
   __shared__ int32_t s_cta_total[kMaxCluster];
 
   int nthreads, tid, group;
@@ -149,7 +224,9 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
   const int lane = tid & 31;
   const int warp = tid >> 5;
   int32_t* gsmem = smem + group * p.smem_group;
-  int32_t* s_wt = gsmem + p.smem_wt;  // [NC][32] warp totals
+  int32_t* s_tbl = gsmem;
+  int32_t* s_wt = gsmem + p.smem_wt;
+  int32_t* s_tile = gsmem + p.smem_tile;
   pdl_launch_dependents();
 
   const int c0 = crank * p.slice;
@@ -173,141 +250,84 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
   pdl_wait();  // everything below may read what the previous grid wrote
 
   const int32_t req = __ldg(p.req_ids + row);
-  int32_t* s_tbl = gsmem;
-  const bool tok_vec = (reinterpret_cast<uintptr_t>(tok) & 15u) == 0;
-  int32_t val[NC][4];
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const int col = 4 * (i * nthreads + tid);
-    if (tok_vec && col + 4 <= len) {
-      const int4 q = __ldg(reinterpret_cast<const int4*>(tok + col));
-      val[i][0] = q.x;
-      val[i][1] = q.y;
-      val[i][2] = q.z;
-      val[i][3] = q.w;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) val[i][j] = (col + j < len) ? __ldg(tok + col + j) : -1;
-    }
-  }
+  const int col = tid * G;  // this thread's first column inside the slice
+  int32_t v[G];
+  load_run<G>(tok + col, len - col, v);
+  const uint32_t tw = p.table_width;
+  // Staged table: speculate that row r belongs to request r (one selection
+  // row per request, in order) and load that table row in the same wave as
+  // the tokens; it is repaired below once the request id is known.
+  const int64_t spec = row < p.table_rows ? row : 0;
+  int32_t t0 = 0;
   if constexpr (STAGE) {
-    // Speculate that row r belongs to request r (one selection row per
-    // request, in order): load that table row in the same wave as the tokens
-    // and keep it in shared memory. It is read only after the first barrier
-    // below, so its latency hides behind the tokens' and the ballots.
-    if (active && row < p.table_rows) {
-      const int32_t* srow = p.table + row * p.table_width;
-      for (int e = tid; e < static_cast<int>(p.table_width); e += nthreads) s_tbl[e] = __ldg(srow + e);
-    }
+    if (static_cast<uint32_t>(tid) < tw) t0 = __ldg(p.table + spec * tw + tid);
   }
 
   const bool req_ok = req >= 0 && static_cast<int64_t>(req) < p.table_rows;
-  if (!req_ok && p.status != nullptr && tid == 0) {
+  if (!req_ok && p.status != nullptr && tid == 0 && active) {
     *reinterpret_cast<volatile int32_t*>(p.status) = SILKERN_STATUS_BAD_REQUEST;
   }
-  const int32_t* trow = p.table + static_cast<int64_t>(req_ok ? req : 0) * p.table_width;
-  if constexpr (STAGE) {
-    if (req_ok && static_cast<int64_t>(req) != row) {  // the same for every thread of the row group
-      // Repair: each thread overwrites exactly the entries it staged above.
-      for (int e = tid; e < static_cast<int>(p.table_width); e += nthreads) s_tbl[e] = __ldg(trow + e);
-    }
-  }
+  const int32_t* trow = p.table + static_cast<int64_t>(req_ok ? req : 0) * tw;
+  // A row whose request id is outside the table keeps no element.
+  const uint32_t twidth = req_ok ? tw : 0u;
+  const uint32_t limit = req_ok ? p.local_limit : 0u;
 
-  // Ownership, deinterleave and the logical block of token t; true when t is
-  // valid here. A row whose request id is outside the table keeps no element
-  // (table width 0).
-  const uint32_t twidth = req_ok ? p.table_width : 0u;
-  auto map_token = [&](int32_t t, uint32_t* lb, uint32_t* local) -> bool {
-    const uint32_t u = static_cast<uint32_t>(t);
+  // Map every element: bit j of `bits` marks a valid one, and v[j] becomes
+  // its local position. Unstaged, its block-table entry is requested here as
+  // well (an invalid element reads entry 0 of the row, branch-free, and never
+  // uses it) into blk[j], so the gather's round trip overlaps the scan.
+  uint32_t bits = 0;
+  int32_t blk[STAGE ? 1 : G];
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const uint32_t u = static_cast<uint32_t>(v[j]);
+    uint32_t lb, local;
+    bool ok;
     if constexpr (MODE == kModePow2Il1) {
-      // interleave 1: local = t >> log2(dcp), owner = t & (dcp - 1). The host
-      // checked 2^(31 - lb_shift) >= table_width, so lb < table_width also
-      // rejects negative tokens.
-      *local = u >> p.group_shift;
-      *lb = u >> p.lb_shift;
-      return *lb < twidth && (u & p.dcp_mask) == p.dcp_rank;
+      // x = t - rank is a multiple of dcp_size exactly when this rank owns
+      // t, and then rotating x right by log2(dcp_size) gives t's local
+      // position. Otherwise (t not owned, t < rank, or t negative) the
+      // rotation leaves a result of at least 2^(31 - log2(dcp_size)), which
+      // the host keeps local_limit at or below; so one compare tests
+      // ownership, sign and lb < table_width together.
+      const uint32_t x = u - p.dcp_rank;
+      local = __funnelshift_r(x, x, p.dcp_shift);
+      lb = local >> p.bs_shift;
+      ok = local < limit;
     } else if constexpr (MODE == kModePow2) {
-      *local = ((u >> p.group_shift) << p.il_shift) | (u & p.il_mask);
-      *lb = *local >> p.bs_shift;
-      return t >= 0 && ((u >> p.il_shift) & p.dcp_mask) == p.dcp_rank && *lb < twidth;
+      local = ((u >> p.group_shift) << p.il_shift) | (u & p.il_mask);
+      lb = local >> p.bs_shift;
+      ok = static_cast<int32_t>(u) >= 0 && ((u >> p.il_shift) & p.dcp_mask) == p.dcp_rank && lb < twidth;
     } else {
       const uint32_t q1 = fastdiv(u, p.div_il);   // t / interleave
       const uint32_t q2 = fastdiv(q1, p.div_dcp);  // t / (dcp_size * interleave)
-      *local = q2 * p.interleave + (u - q1 * p.interleave);
-      *lb = fastdiv(*local, p.div_bs);
-      return t >= 0 && q1 - q2 * p.dcp_size == p.dcp_rank && *lb < twidth;  // owner == rank
+      local = q2 * p.interleave + (u - q1 * p.interleave);
+      lb = fastdiv(local, p.div_bs);
+      ok = static_cast<int32_t>(u) >= 0 && q1 - q2 * p.dcp_size == p.dcp_rank && lb < twidth;
     }
-  };
-  // physical = table[lb] * block_size + (local - lb * block_size), one
-  // multiply-add, wrapping like the reference's int32 lanes.
-  auto physical = [&](int32_t blk, uint32_t lb, uint32_t local) -> int32_t {
-    return static_cast<int32_t>((static_cast<uint32_t>(blk) - lb) * p.block_size + local);
-  };
-
-  // Map every element: bits[i] marks the valid ones. Gathering from global
-  // memory, val becomes the physical slot here (or -1; compacting calls
-  // never store an invalid element); with a staged table row, val keeps the
-  // token until the table is read after the first barrier.
-  uint32_t bits[NC];
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    uint32_t b = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t lb, local;
-      const bool ok = map_token(val[i][j], &lb, &local);
-      if constexpr (!STAGE) {
-        // branch-free: an invalid token reads entry 0 of the row, unused
-        const int32_t blk = __ldg(trow + (ok ? lb : 0u));
-        val[i][j] = ok ? physical(blk, lb, local) : (COMPACT ? 0 : -1);
-      }
-      b |= ok ? (1u << j) : 0u;
-    }
-    bits[i] = b;
+    if constexpr (!STAGE) blk[j] = __ldg(trow + (ok ? lb : 0u));
+    v[j] = static_cast<int32_t>(local);
+    bits |= ok ? (1u << j) : 0u;
   }
 
-  // Lane prefix inside the warp from three ballots over the per-lane count
-  // (0..4, three bits), warp totals through shared memory, per chunk.
-  int lane_pre[NC];
-  const uint32_t lt = lanemask_lt();
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const uint32_t c = __popc(bits[i]);
-    const uint32_t b0 = __ballot_sync(kFull, c & 1u);
-    const uint32_t b1 = __ballot_sync(kFull, c & 2u);
-    const uint32_t b2 = __ballot_sync(kFull, c & 4u);
-    lane_pre[i] = __popc(b0 & lt) + 2 * __popc(b1 & lt) + 4 * __popc(b2 & lt);
-    if (lane == 0) s_wt[i * 32 + warp] = __popc(b0) + 2 * __popc(b1) + 4 * __popc(b2);
-  }
-  __syncthreads();
+  // Exclusive prefix of this thread's first element inside the CTA.
+  const uint32_t c = __popc(bits);
+  const int excl = warp_exclusive<count_bits(G)>(c);
   if constexpr (STAGE) {
-    // the staged table row is complete: translate the valid tokens
-#pragma unroll
-    for (int i = 0; i < NC; ++i) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        int32_t phys = COMPACT ? 0 : -1;
-        if (bits[i] & (1u << j)) {
-          uint32_t lb, local;
-          (void)map_token(val[i][j], &lb, &local);
-          phys = physical(s_tbl[lb], lb, local);
-        }
-        val[i][j] = phys;
-      }
+    // Repair a wrong speculation (the same decision for the whole row group:
+    // each thread overwrites exactly the entries it loaded), then publish
+    // the staged row; the barrier below makes it visible to the group.
+    if (req_ok && req != spec && static_cast<uint32_t>(tid) < tw) t0 = __ldg(trow + tid);
+    if (static_cast<uint32_t>(tid) < tw) s_tbl[tid] = t0;
+    for (uint32_t e = static_cast<uint32_t>(tid + nthreads); e < tw; e += static_cast<uint32_t>(nthreads)) {
+      s_tbl[e] = __ldg(trow + e);
     }
   }
-
-  // Exclusive base of (chunk i, this warp) inside the CTA: all earlier chunks,
-  // then the earlier warps of chunk i.
-  int base[NC];
-  int run = 0;
-#pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const int x = lane < nwarps ? s_wt[i * 32 + lane] : 0;
-    base[i] = run + __reduce_add_sync(kFull, lane < warp ? x : 0);
-    run += __reduce_add_sync(kFull, x);
-  }
-  const int cta_total = run;
+  if (lane == 31) s_wt[warp] = excl + static_cast<int>(c);
+  __syncthreads();
+  const int x = lane < nwarps ? s_wt[lane] : 0;
+  const int pos = __reduce_add_sync(kFull, lane < warp ? x : 0) + excl;
+  const int cta_total = __reduce_add_sync(kFull, x);
 
   int row_off = 0;
   int row_total = cta_total;
@@ -319,93 +339,90 @@ __global__ void __launch_bounds__((NC == 1 && !CLUSTER) ? kMaxCtaThreads : kMaxT
     cluster_wait_acquire();  // phase 1: every CTA's total is in s_cta_total
     row_total = 0;
     for (int r = 0; r < cs; ++r) {
-      const int v = s_cta_total[r];
-      row_off += r < crank ? v : 0;
-      row_total += v;
+      const int w = s_cta_total[r];
+      row_off += r < crank ? w : 0;
+      row_total += w;
     }
   }
 
-  // Hierarchical: the CTA-local exclusive position of the element in each
-  // tile's first column is that tile's offset (before the row offset), staged
-  // in shared memory ahead of a barrier that precedes the publishing loop.
-  int32_t* s_tile = gsmem + p.smem_tile;
-  const bool tiles = p.tile_shift >= 0;
-  if (tiles) {
-    // Tiles are multiples of 64 columns and chunks start at multiples of 4,
-    // so a tile can only start at a chunk's first column (prefix 0 in-lane).
-    const int tmask = (1 << p.tile_shift) - 1;
+  // Paged translation: physical = table[lb] * block_size + (local mod
+  // block_size), one multiply-add that wraps like the reference's int32
+  // lanes; invalid elements become -1 (never stored when compacting).
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int col = 4 * (i * nthreads + tid);
-      if (col < len && (col & tmask) == 0) s_tile[col >> p.tile_shift] = base[i] + lane_pre[i];
+  for (int j = 0; j < G; ++j) {
+    const uint32_t local = static_cast<uint32_t>(v[j]);
+    uint32_t lb, off;
+    if constexpr (MODE == kModeGeneral) {
+      lb = fastdiv(local, p.div_bs);
+      off = local - lb * p.block_size;
+    } else {
+      lb = local >> p.bs_shift;
+      off = local & p.bs_mask;
     }
+    const bool ok = (bits >> j) & 1u;
+    int32_t b = 0;
+    if constexpr (STAGE) {
+      if (ok) b = s_tbl[lb];
+    } else {
+      b = blk[j];
+    }
+    v[j] = ok ? static_cast<int32_t>(static_cast<uint32_t>(b) * p.block_size + off) : -1;
   }
+
+  // Hierarchical: the CTA-local exclusive position of each tile's first
+  // column is that tile's offset (before the row offset). Tiles are
+  // multiples of 64 columns and G divides 64, so every tile starts at some
+  // thread's first column.
+  const bool tiles = p.tile_shift >= 0;
+  if (tiles && col < len && (col & ((1 << p.tile_shift) - 1)) == 0) s_tile[col >> p.tile_shift] = pos;
 
   int32_t* orow = p.out + row * p.width;
-  if constexpr (COMPACT) {
-    if constexpr (!CLUSTER) {
-      // The whole row is this CTA's: each survivor goes straight to its final
-      // position, and the granules at or past cta_total are filled with -1.
-      // Every output element is written once.
+  if constexpr (COMPACT && !CLUSTER) {
+    // Stage each survivor at its position in the row; then each thread
+    // writes its own columns, survivors below the count and -1 from it on.
+    int32_t* s_out = gsmem + p.smem_out;
+    int k = pos;
 #pragma unroll
-      for (int i = 0; i < NC; ++i) {
-        int32_t* dst = orow + base[i] + lane_pre[i];
-        int k = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (bits[i] & (1u << j)) dst[k] = val[i][j];
-          k += (bits[i] >> j) & 1u;
-        }
-      }
-      if (tiles) __syncthreads();  // s_tile is complete
-      const bool out_vec = (reinterpret_cast<uintptr_t>(orow) & 15u) == 0;
-#pragma unroll
-      for (int i = 0; i < NC; ++i) {
-        const int col = 4 * (i * nthreads + tid);
-        if (col < len && col + 4 > cta_total) {  // this granule holds part of the -1 tail
-          if (out_vec && col >= cta_total && col + 4 <= len) {
-            *reinterpret_cast<int4*>(orow + col) = make_int4(-1, -1, -1, -1);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (col + j >= cta_total && col + j < len) orow[col + j] = -1;
-            }
-          }
-        }
-      }
-    } else {
-      // Each survivor straight to its final position (this CTA's run starts at
-      // the row offset from the cluster exchange), then the -1 tail of the
-      // CTA's own slice.
-#pragma unroll
-      for (int i = 0; i < NC; ++i) {
-        int32_t* dst = orow + row_off + base[i] + lane_pre[i];
-        int k = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (bits[i] & (1u << j)) dst[k] = val[i][j];
-          k += (bits[i] >> j) & 1u;
-        }
-      }
-      if (tiles) __syncthreads();  // s_tile is complete
-      fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
+    for (int j = 0; j < G; ++j) {
+      if ((bits >> j) & 1u) s_out[k] = v[j];
+      k += static_cast<int>((bits >> j) & 1u);
     }
-  } else {
-    if (tiles) __syncthreads();  // s_tile is complete
-    int32_t* dst = orow + c0;
-    const bool out_vec = (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+    __syncthreads();  // s_out and s_tile are complete
+    if (col < len) {
+      int32_t w[G];
+      if (col + G <= cta_total) {
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int col = 4 * (i * nthreads + tid);
-      if (out_vec && col + 4 <= len) {
-        *reinterpret_cast<int4*>(dst + col) = make_int4(val[i][0], val[i][1], val[i][2], val[i][3]);
+        for (int i = 0; i < G / 4; ++i) {
+          const int4 q = reinterpret_cast<const int4*>(s_out + col)[i];
+          w[4 * i + 0] = q.x;
+          w[4 * i + 1] = q.y;
+          w[4 * i + 2] = q.z;
+          w[4 * i + 3] = q.w;
+        }
+      } else if (col >= cta_total) {
+#pragma unroll
+        for (int j = 0; j < G; ++j) w[j] = -1;
       } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (col + j < len) dst[col + j] = val[i][j];
-        }
+        for (int j = 0; j < G; ++j) w[j] = col + j < cta_total ? s_out[col + j] : -1;
       }
+      store_run<G>(orow + col, len - col, w);
     }
+  } else if constexpr (COMPACT) {
+    // Across a cluster each survivor goes straight to its final position
+    // after the CTA's row offset; then the -1 tail of the CTA's own slice.
+    int32_t* dst = orow + row_off + pos;
+    int k = 0;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      if ((bits >> j) & 1u) dst[k] = v[j];
+      k += static_cast<int>((bits >> j) & 1u);
+    }
+    fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
+    if (tiles) __syncthreads();  // s_tile is complete
+  } else {
+    if (tiles) __syncthreads();  // s_tile is complete
+    if (col < len) store_run<G>(orow + c0 + col, len - col, v);
   }
 
   if (tiles) {
@@ -459,38 +476,36 @@ namespace {
 
 using KernelFn = void (*)(Params);
 
-template <int NC, bool CLUSTER, int MODE, bool STAGE>
-KernelFn pick_compact(bool compact) {
-  return compact ? localize_kernel<NC, CLUSTER, MODE, STAGE, true>
-                 : localize_kernel<NC, CLUSTER, MODE, STAGE, false>;
+template <int G, bool CLUSTER, int MODE, bool COMPACT>
+KernelFn pick_stage(bool stage) {
+  return stage ? localize_kernel<G, CLUSTER, MODE, COMPACT, true> : localize_kernel<G, CLUSTER, MODE, COMPACT, false>;
 }
 
-template <int NC, bool CLUSTER, int MODE>
-KernelFn pick_stage(bool stage, bool compact) {
-  return stage ? pick_compact<NC, CLUSTER, MODE, true>(compact)
-               : pick_compact<NC, CLUSTER, MODE, false>(compact);
+template <int G, bool CLUSTER, int MODE>
+KernelFn pick_compact(bool compact, bool stage) {
+  return compact ? pick_stage<G, CLUSTER, MODE, true>(stage) : pick_stage<G, CLUSTER, MODE, false>(stage);
 }
 
-template <int NC, bool CLUSTER>
-KernelFn pick_mode(int mode, bool stage, bool compact) {
+template <int G, bool CLUSTER>
+KernelFn pick_mode(int mode, bool compact, bool stage) {
   switch (mode) {
-    case kModePow2Il1: return pick_stage<NC, CLUSTER, kModePow2Il1>(stage, compact);
-    case kModePow2: return pick_stage<NC, CLUSTER, kModePow2>(stage, compact);
-    default: return pick_stage<NC, CLUSTER, kModeGeneral>(stage, compact);
+    case kModePow2Il1: return pick_compact<G, CLUSTER, kModePow2Il1>(compact, stage);
+    case kModePow2: return pick_compact<G, CLUSTER, kModePow2>(compact, stage);
+    default: return pick_compact<G, CLUSTER, kModeGeneral>(compact, stage);
   }
 }
 
-template <int NC>
-KernelFn pick_for_nc(bool cluster, int mode, bool stage, bool compact) {
-  return cluster ? pick_mode<NC, true>(mode, stage, compact) : pick_mode<NC, false>(mode, stage, compact);
+template <int G>
+KernelFn pick_for_run(bool cluster, int mode, bool compact, bool stage) {
+  return cluster ? pick_mode<G, true>(mode, compact, stage) : pick_mode<G, false>(mode, compact, stage);
 }
 
-KernelFn pick_kernel(int nc, bool cluster, int mode, bool stage, bool compact) {
-  switch (nc) {
-    case 1: return pick_for_nc<1>(cluster, mode, stage, compact);
-    case 2: return pick_for_nc<2>(cluster, mode, stage, compact);
-    case 4: return pick_for_nc<4>(cluster, mode, stage, compact);
-    case 8: return pick_for_nc<8>(cluster, mode, stage, compact);
+KernelFn pick_kernel(int run, bool cluster, int mode, bool compact, bool stage) {
+  switch (run) {
+    case 4: return pick_for_run<4>(cluster, mode, compact, stage);
+    case 8: return pick_for_run<8>(cluster, mode, compact, stage);
+    case 16: return pick_for_run<16>(cluster, mode, compact, stage);
+    case 32: return pick_for_run<32>(cluster, mode, compact, stage);
     default: return nullptr;
   }
 }
@@ -539,7 +554,10 @@ struct Request {
   cudaStream_t stream;
 };
 
-int validate(const Request& r) {
+// Argument checks shared by every entry point, before anything is launched.
+// need_tile_buffers = false skips only the check that the tile workspace
+// pointers are set (the allocation-free entry point supplies its own).
+int validate(const Request& r, bool need_tile_buffers = true) {
   if (!r.req_ids || !r.table || !r.tokens || !r.out || !r.counts) return SILKERN_E_NULL;
   if (r.batch < 1 || r.width < 1 || r.width > SILKERN_MAX_ROW_WIDTH || r.table_rows < 1 ||
       r.table_width < 1 || r.table_width > INT32_MAX || r.batch > (int64_t{1} << 27)) {
@@ -552,7 +570,7 @@ int validate(const Request& r) {
         !is_pow2(static_cast<uint32_t>(r.tile_size))) {
       return SILKERN_E_TILE;
     }
-    if (!r.tile_counts || !r.tile_offsets) return SILKERN_E_NULL;
+    if (need_tile_buffers && (!r.tile_counts || !r.tile_offsets)) return SILKERN_E_NULL;
   }
   const int64_t bw = r.batch * r.width;
   const int64_t tiles = r.tile_size ? r.batch * ((r.width + r.tile_size - 1) / r.tile_size) : 0;
@@ -578,12 +596,15 @@ int validate(const Request& r) {
 struct Geometry {
   int cluster;
   int slice;
-  int threads;  // per row group
-  int nc;
+  int threads;  // per row group (per CTA with a cluster)
+  int run;      // columns per thread
   bool stage;
   bool prefetch;
   int rows_per_cta;   // row groups per CTA (1 with a cluster)
   int64_t row_ctas;   // CTAs over the batch (times `cluster` for the grid)
+  // dynamic shared memory per row group, in ints: [table stage][staged
+  // output][warp totals][tile offsets], every part 16-byte aligned
+  int smem_out, smem_wt, smem_tile, smem_group;
 };
 
 uint32_t next_pow2(uint32_t v) {
@@ -616,31 +637,37 @@ void smem_limits(int* per_sm, int* reserved) {
   *reserved = cache_res[dev];
 }
 
-// Chunks of four columns per thread and threads for `slice` columns: up to
-// max_threads threads with one chunk each, then more chunks per thread over
-// at most kMaxThreads threads (short per-thread dependency chains measured
-// faster than fewer, longer ones).
-bool fit_slice(int slice, int nc_req, int max_threads, int* nc, int* threads) {
-  const int granules = (slice + 3) / 4;
-  int c = 1;
-  if (nc_req > 0) {
-    c = nc_req;
-  } else if (granules > max_threads) {
-    // more than one chunk per thread: groups of at most kMaxThreads
-    c = 2;
-    while (granules > c * kMaxThreads) c *= 2;
+// Columns per thread and threads for `slice` columns: the shortest run that
+// covers the slice with at most kMaxThreads threads, starting from 8 columns
+// on one CTA and 16 across a cluster (measured the faster starts), unless
+// run_req pins it (4, 8, 16 or 32). Threads are a whole number of warps; a
+// row group (no cluster) is a power of two of them.
+bool fit_slice(int slice, int run_req, bool cluster, int* run, int* threads) {
+  int g = run_req;
+  if (g == 0) {
+    g = cluster ? 16 : 8;
+    while (g < 32 && (slice + g - 1) / g > kMaxThreads) g *= 2;
   }
-  const int limit = c == 1 ? max_threads : kMaxThreads;
-  if (c > 8 || granules > c * limit) return false;
-  int t = (granules + c - 1) / c;
+  int t = (slice + g - 1) / g;
   t = (t + 31) / 32 * 32;
-  *nc = c;
+  if (!cluster) t = static_cast<int>(next_pow2(static_cast<uint32_t>(t)));
+  if (t > kMaxThreads) return false;
+  *run = g;
   *threads = t;
   return true;
 }
 
-int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefetch_req, int nc_req,
-                    Geometry* g) {
+void layout_smem(const Request& r, bool compact, Geometry* g) {
+  const int ntiles_cta = r.tile_size ? (g->slice + r.tile_size - 1) / r.tile_size : 0;
+  const int stage_ints = g->stage ? static_cast<int>((r.table_width + 3) / 4 * 4) : 0;
+  g->smem_out = stage_ints;
+  g->smem_wt = g->smem_out + ((compact && g->cluster == 1) ? (g->slice + 3) / 4 * 4 : 0);
+  g->smem_tile = g->smem_wt + 32;
+  g->smem_group = (g->smem_tile + ntiles_cta + 3) / 4 * 4;
+}
+
+int choose_geometry(const Request& r, bool compact, int cluster_req, int stage_req, int prefetch_req,
+                    int run_req, Geometry* g) {
   const int width = static_cast<int>(r.width);
   int cs;
   int slice;
@@ -677,40 +704,43 @@ int choose_geometry(const Request& r, int cluster_req, int stage_req, int prefet
         cs *= 2;
       }
     }
+    // Slices start on 64-column boundaries, so every run keeps the row's
+    // alignment.
     slice = (width + cs - 1) / cs;
-    slice = (slice + 3) / 4 * 4;
+    slice = (slice + 63) / 64 * 64;
     cs = (width + slice - 1) / slice;
   }
   if (cluster_req > 0 && cs != cluster_req) return SILKERN_E_GEOMETRY;
   if (cs < 1 || cs > kMaxCluster) return SILKERN_E_GEOMETRY;
-  // A cluster CTA or a row group has at most kMaxThreads threads (cluster
-  // CTAs of 1024 threads under a 32-register bound measured slower); short
-  // rows share a CTA (row groups, below).
-  if (!fit_slice(slice, nc_req, kMaxThreads, &g->nc, &g->threads)) return SILKERN_E_GEOMETRY;
+  if (!fit_slice(slice, run_req, cs > 1, &g->run, &g->threads)) return SILKERN_E_GEOMETRY;
   g->cluster = cs;
   g->slice = slice;
   g->rows_per_cta = 1;
   g->row_ctas = r.batch;
   if (cs == 1) {
-    // Row groups: a power-of-two group per row; one-chunk rows are packed
-    // into CTAs of up to 1024 threads, with the rows spread over at most one
-    // CTA per SM.
-    g->threads = static_cast<int>(next_pow2(static_cast<uint32_t>(g->threads)));
-    if (g->nc == 1) {
-      int64_t max_rows = kMaxCtaThreads / g->threads;
-      if (max_rows > kMaxRowGroups) max_rows = kMaxRowGroups;
-      int64_t ctas = r.batch < sm_count() ? r.batch : sm_count();
-      int64_t rows = (r.batch + ctas - 1) / ctas;
-      if (rows > max_rows) {
-        rows = max_rows;
-        ctas = (r.batch + rows - 1) / rows;
-      }
-      g->rows_per_cta = static_cast<int>(rows);
-      g->row_ctas = ctas;
+    // Row groups: rows are packed into CTAs of up to kMaxThreads threads and
+    // spread over at most one CTA per SM.
+    const int64_t max_rows = kMaxThreads / g->threads;
+    int64_t ctas = r.batch < sm_count() ? r.batch : sm_count();
+    int64_t rows = (r.batch + ctas - 1) / ctas;
+    if (rows > max_rows) {
+      rows = max_rows;
+      ctas = (r.batch + rows - 1) / rows;
     }
+    g->rows_per_cta = static_cast<int>(rows);
+    g->row_ctas = ctas;
   }
+  // Table stage: on request (rows up to kTableStageMax entries), or by
+  // default whenever the row fits and the CTA's shared memory stays modest.
   if (stage_req == 1 && r.table_width > kTableStageMax) return SILKERN_E_GEOMETRY;
-  g->stage = stage_req == 1;
+  g->stage = stage_req == 1 || (stage_req < 0 && r.table_width <= kTableStageMax);
+  layout_smem(r, compact, g);
+  if (stage_req < 0 && g->stage &&
+      static_cast<int64_t>(g->smem_group) * 4 * g->rows_per_cta > kStageSmemMax) {
+    g->stage = false;
+    layout_smem(r, compact, g);
+  }
+  if (static_cast<int64_t>(g->smem_group) * 4 * g->rows_per_cta > kSmemMax) return SILKERN_E_GEOMETRY;
   const int64_t table_bytes = r.table_rows * r.table_width * 4;
   const bool aligned = (reinterpret_cast<uintptr_t>(r.table) & 15u) == 0;
   const bool possible = aligned && table_bytes >= 16 && table_bytes <= (int64_t{1} << 32);
@@ -754,11 +784,12 @@ int allow_large_smem(KernelFn fn, size_t bytes) {
   return SILKERN_OK;
 }
 
-int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req, int nc_req) {
+int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req, int run_req) {
   int rc = validate(r);
   if (rc != SILKERN_OK) return rc;
+  const bool compact = r.compact_flag != 0 && r.dcp_size > 1;
   Geometry g;
-  rc = choose_geometry(r, cluster_req, stage_req, prefetch_req, nc_req, &g);
+  rc = choose_geometry(r, compact, cluster_req, stage_req, prefetch_req, run_req, &g);
   if (rc != SILKERN_OK) return rc;
 
   Params p{};
@@ -775,7 +806,6 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req, i
   p.width = static_cast<int32_t>(r.width);
   p.slice = g.slice;
   p.cluster = g.cluster;
-  p.compact = (r.compact_flag != 0 && r.dcp_size > 1) ? 1 : 0;
   p.tile_shift = r.tile_size ? static_cast<int32_t>(log2_exact(static_cast<uint32_t>(r.tile_size))) : -1;
   p.tiles_per_row = r.tile_size ? static_cast<int32_t>((r.width + r.tile_size - 1) / r.tile_size) : 0;
   const int64_t grid = g.row_ctas * g.cluster;
@@ -803,30 +833,31 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req, i
   int mode = kModeGeneral;
   if (pow2) {
     p.il_shift = log2_exact(p.interleave);
-    p.group_shift = p.il_shift + log2_exact(p.dcp_size);
+    p.dcp_shift = log2_exact(p.dcp_size);
+    p.group_shift = p.il_shift + p.dcp_shift;
     p.bs_shift = log2_exact(p.block_size);
-    p.lb_shift = p.group_shift + p.bs_shift;
     p.il_mask = p.interleave - 1;
     p.dcp_mask = p.dcp_size - 1;
     p.bs_mask = p.block_size - 1;
     mode = kModePow2;
-    // interleave 1 and a table no wider than 2^(31 - lb_shift): one unsigned
-    // compare of t >> lb_shift against the width rejects negative tokens too.
-    if (p.interleave == 1 && p.lb_shift <= 30 &&
-        static_cast<uint64_t>(p.table_width) <= (uint64_t{1} << (31 - p.lb_shift))) {
+    if (p.interleave == 1) {
+      // A valid element's local position is below table_width * block_size
+      // (lb < table_width) and, since t < 2^31, below 2^(31 - log2(dcp_size));
+      // every element this rank does not own, or that is negative, rotates
+      // to at least 2^(31 - log2(dcp_size)).
+      const uint64_t by_table = static_cast<uint64_t>(r.table_width) << p.bs_shift;
+      const uint64_t by_sign = uint64_t{1} << (31 - p.dcp_shift);
+      p.local_limit = static_cast<uint32_t>(by_table < by_sign ? by_table : by_sign);
       mode = kModePow2Il1;
     }
   }
 
-  KernelFn fn = pick_kernel(g.nc, g.cluster > 1, mode, g.stage, p.compact != 0);
+  KernelFn fn = pick_kernel(g.run, g.cluster > 1, mode, compact, g.stage);
   if (fn == nullptr) return SILKERN_E_GEOMETRY;
-  const int ntiles_cta = r.tile_size ? (g.slice + r.tile_size - 1) / r.tile_size : 0;
-  // dynamic shared memory per row group: [table stage][warp totals][tile
-  // offsets], every part 16-byte aligned
-  const int stage_ints = g.stage ? static_cast<int>((r.table_width + 3) / 4 * 4) : 0;
-  p.smem_wt = stage_ints;
-  p.smem_tile = p.smem_wt + g.nc * 32;
-  p.smem_group = (p.smem_tile + ntiles_cta + 3) / 4 * 4;
+  p.smem_out = g.smem_out;
+  p.smem_wt = g.smem_wt;
+  p.smem_tile = g.smem_tile;
+  p.smem_group = g.smem_group;
   size_t smem = sizeof(int32_t) * static_cast<size_t>(p.smem_group) * static_cast<size_t>(g.rows_per_cta);
   if (g.cluster == 1 && grid <= sm_count()) {
     // At most two CTAs of this kernel per SM: the running call and the next
@@ -922,17 +953,58 @@ extern "C" int silkern_localize_explicit_v1(
                   tile_counts_ws, tile_offsets_ws, batch, width, block_size, dcp_size, dcp_rank,
                   dcp_interleave, compact_valid_to_front, tile_size, status,
                   static_cast<cudaStream_t>(stream)};
-  return silkern::launch(r, cluster_size, stage_table, prefetch_table, chunks_per_thread);
+  return silkern::launch(r, cluster_size, stage_table, prefetch_table, 4 * chunks_per_thread);
 }
 
 namespace silkern {
 namespace {
 
-// Device address of g_noalloc_tiles on the current device, looked up once per
-// device (with that device current) and cached.
+// The driver's cuCtxGetCurrent and cuCtxGetId, reached through the runtime
+// so the library needs no link-time dependency on libcuda. A context's id is
+// unique for the life of the process, even when a reset frees the context
+// and a new one takes its place (and perhaps its handle).
+using CtxGetCurrentFn = int (*)(void**);
+using CtxGetIdFn = int (*)(void*, unsigned long long*);
+
+bool current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult found = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 12000, cudaEnableDefault, &found) ==
+            cudaSuccess &&
+        found == cudaDriverEntryPointSuccess) {
+      get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    }
+    fn = nullptr;
+    found = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &fn, 12000, cudaEnableDefault, &found) ==
+            cudaSuccess &&
+        found == cudaDriverEntryPointSuccess) {
+      get_id = reinterpret_cast<CtxGetIdFn>(fn);
+    }
+    (void)cudaGetLastError();
+  });
+  if (get_current == nullptr || get_id == nullptr) return false;
+  void* ctx = nullptr;
+  if (get_current(&ctx) != 0 || ctx == nullptr) return false;
+  return get_id(ctx, id) == 0;
+}
+
+// Device address of g_noalloc_tiles in the current device's context. It is
+// looked up with cudaGetSymbolAddress the first time a device (with that
+// device current) calls, and again whenever the device's context has changed
+// since (a cudaDeviceReset, for one), so a cached address never outlives its
+// context. Without the driver's context ids it is looked up on every call.
 int noalloc_scratch(int32_t** out) {
+  struct Slot {
+    int32_t* ptr;
+    unsigned long long ctx_id;
+  };
   static std::mutex mu;
-  static int32_t* cache[64] = {nullptr};
+  static Slot cache[64] = {};
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) {
@@ -941,16 +1013,19 @@ int noalloc_scratch(int32_t** out) {
   }
   if (dev < 0 || dev >= 64) return SILKERN_E_SCRATCH;
   std::lock_guard<std::mutex> lock(mu);
-  if (cache[dev] == nullptr) {
-    void* ptr = nullptr;
-    err = cudaGetSymbolAddress(&ptr, g_noalloc_tiles);
-    if (err != cudaSuccess || ptr == nullptr) {
-      (void)cudaGetLastError();
-      return err != cudaSuccess ? -static_cast<int>(err) : SILKERN_E_SCRATCH;
-    }
-    cache[dev] = static_cast<int32_t*>(ptr);
+  unsigned long long id = 0;
+  if (cache[dev].ptr != nullptr && current_context_id(&id) && id == cache[dev].ctx_id) {
+    *out = cache[dev].ptr;
+    return SILKERN_OK;
   }
-  *out = cache[dev];
+  void* ptr = nullptr;
+  err = cudaGetSymbolAddress(&ptr, g_noalloc_tiles);  // makes the device's context current if needed
+  if (err != cudaSuccess || ptr == nullptr) {
+    (void)cudaGetLastError();
+    return err != cudaSuccess ? -static_cast<int>(err) : SILKERN_E_SCRATCH;
+  }
+  cache[dev] = current_context_id(&id) ? Slot{static_cast<int32_t*>(ptr), id} : Slot{nullptr, 0};
+  *out = static_cast<int32_t*>(ptr);
   return SILKERN_OK;
 }
 
@@ -962,19 +1037,20 @@ extern "C" int silkern_localize_hierarchical_noalloc_v1(
     const int32_t* tokens, int32_t* out, int32_t* counts, int64_t batch, int64_t width,
     int32_t block_size, int32_t dcp_size, int32_t dcp_rank, int32_t dcp_interleave,
     int32_t compact_valid_to_front, int32_t tile_size, int32_t* status, void* stream) {
-  if (tile_size < SILKERN_MIN_TILE_SIZE || tile_size > SILKERN_MAX_TILE_SIZE ||
-      !silkern::is_pow2(static_cast<uint32_t>(tile_size))) {
-    return SILKERN_E_TILE;
-  }
-  if (batch < 1 || width < 1 || width > SILKERN_MAX_ROW_WIDTH) return SILKERN_E_SHAPE;
+  if (tile_size == 0) return SILKERN_E_TILE;
+  Request r{req_ids, block_table, table_rows, table_width, tokens, out, counts, nullptr, nullptr,
+            batch, width, block_size, dcp_size, dcp_rank, dcp_interleave, compact_valid_to_front,
+            tile_size, status, static_cast<cudaStream_t>(stream)};
+  // The same checks, in the same order, as the workspace entry point; the
+  // static array's limit comes after them.
+  int rc = silkern::validate(r, /*need_tile_buffers=*/false);
+  if (rc != SILKERN_OK) return rc;
   if (batch * ((width + tile_size - 1) / tile_size) > SILKERN_NOALLOC_MAX_TILES) return SILKERN_E_SCRATCH;
   int32_t* scratch = nullptr;
-  const int rc = silkern::noalloc_scratch(&scratch);
+  rc = silkern::noalloc_scratch(&scratch);
   if (rc != SILKERN_OK) return rc;
-  const Request r{req_ids, block_table, table_rows, table_width, tokens, out, counts, scratch,
-                  scratch + SILKERN_NOALLOC_MAX_TILES, batch, width, block_size, dcp_size, dcp_rank,
-                  dcp_interleave, compact_valid_to_front, tile_size, status,
-                  static_cast<cudaStream_t>(stream)};
+  r.tile_counts = scratch;
+  r.tile_offsets = scratch + SILKERN_NOALLOC_MAX_TILES;
   return silkern::launch(r, 0, -1, -1, 0);
 }
 

@@ -1,6 +1,6 @@
 // Thin inline-PTX wrappers for the sm_90+/sm_100a features the kernels use:
 // programmatic dependent launch, thread-block cluster barriers, distributed
-// shared memory stores and the bulk L2 prefetch.
+// shared memory stores, the bulk L2 prefetch and 256-bit global accesses.
 #pragma once
 
 #include <cstdint>
@@ -63,6 +63,22 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
   uint32_t m;
   asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
   return m;
+}
+
+// 256-bit global load through the non-coherent (read-only) path; ptr 32-byte
+// aligned. Volatile so that it stays after griddepcontrol.wait.
+__device__ __forceinline__ void ld_nc_v8(const int32_t* ptr, int32_t (&v)[8]) {
+  asm volatile("ld.global.nc.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                 "=r"(v[7])
+               : "l"(ptr));
+}
+
+// 256-bit global store; ptr 32-byte aligned.
+__device__ __forceinline__ void st_v8(int32_t* ptr, const int32_t (&v)[8]) {
+  asm volatile("st.global.v8.u32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(ptr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
 }
 
 }  // namespace silkern

@@ -63,6 +63,10 @@ constexpr int64_t kPrefetchBytes = 16384;  // per bulk L2 prefetch
 constexpr int kStreamUnroll = 8;      // 128-column blocks in flight per warp
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
 constexpr int64_t kTopkSmemBudget = 200 * 1024;  // dynamic shared memory per CTA
+// The write pass packs a CTA's selected and valid counts into one int, 16
+// bits each; a candidate list of 8-byte entries within the budget stays
+// below 2^16 entries.
+static_assert(kTopkSmemBudget / 8 < 65536, "candidate counts must fit 16 bits");
 constexpr int kMaxBlocks = SILKERN_TOPK_MAX_WIDTH / kBlockCols;
 constexpr uint32_t kAll = 0xffffffffu;
 // CTA shapes (threads T): 512 threads, two CTAs per SM, when the batch needs
@@ -801,7 +805,7 @@ int topk_launch(const float* logits, int64_t stride, int64_t width, const int32_
   int64_t cap = int64_t{3} * top_k + 2048;
   if (cap > cap_max) cap = cap_max;
   if (cap_req != 0) {
-    if (cap_req > cap_max) return SILKERN_E_GEOMETRY;
+    if (cap_req > cap_max || cap_req >= 65536) return SILKERN_E_GEOMETRY;
     cap = cap_req;
   }
   if (cap < top_k) return SILKERN_E_GEOMETRY;

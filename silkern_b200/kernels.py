@@ -290,7 +290,8 @@ def localize_explicit(
 
     Same outputs as the two public launchers; ``cluster_size`` CTAs per row,
     ``stage_table``/``prefetch_table`` 1, 0 or -1 (library choice),
-    ``chunks_per_thread`` 1, 2, 4, 8 or 0 (library choice). With
+    ``chunks_per_thread`` 1, 2, 4, 8 or 0 (library choice): each thread maps
+    a run of 4 x chunks_per_thread consecutive columns. With
     ``tile_size`` > 0 the hierarchical tile workspace is published. Buffers
     are checked by the C ABI only.
     """

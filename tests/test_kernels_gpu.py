@@ -4,8 +4,8 @@ Bit-exact (set, count and order) against:
 * every golden case recorded from the reference's own ``localize_reference``
   and Triton kernels (tests/golden/golden.json), both arms;
 * the C oracle on seeded inputs, over the launch-geometry space (cluster
-  sizes, table staging, L2 prefetch, power-of-two and general arithmetic,
-  misaligned rows) and at the full benchmark sizes.
+  sizes, columns per thread, table staging, L2 prefetch, power-of-two and
+  general arithmetic, misaligned rows) and at the full benchmark sizes.
 Test names and cases follow the reference's tests/test_kernels_gpu.py.
 """
 
@@ -138,7 +138,7 @@ def _oracle(req, table, tokens, **kw):
     return oracle.localize(req, table, tokens, threads=4, **kw)
 
 
-def _explicit(req, table, tokens, *, cluster, stage, prefetch, tile_size=0, status=None, **kw):
+def _explicit(req, table, tokens, *, cluster, stage, prefetch, chunks=0, tile_size=0, status=None, **kw):
     req, table, tokens = (_cuda(a) for a in (req, table, tokens))
     batch, width = tokens.shape
     out = torch.full_like(tokens, 0x5A5A5A5A)
@@ -149,7 +149,8 @@ def _explicit(req, table, tokens, *, cluster, stage, prefetch, tile_size=0, stat
         tc = torch.empty((batch, tiles), dtype=torch.int32, device=DEV)
         to = torch.empty((batch, tiles), dtype=torch.int32, device=DEV)
     localize_explicit(req, table, tokens, out, counts, cluster_size=cluster, stage_table=stage,
-                      prefetch_table=prefetch, tile_size=tile_size, tile_counts=tc,
+                      prefetch_table=prefetch, chunks_per_thread=chunks, tile_size=tile_size,
+                      tile_counts=tc,
                       tile_offsets=to, status=status, **kw)
     torch.cuda.synchronize()
     tiles_out = None if tc is None else (tc.cpu().numpy(), to.cpu().numpy())
@@ -162,7 +163,7 @@ def _slices_fit(width, cluster, tile_size):
         per = -(-tiles // cluster)
         return -(-tiles // per) == cluster
     slice_ = -(-width // cluster)
-    slice_ = -(-slice_ // 4) * 4
+    slice_ = -(-slice_ // 64) * 64
     return -(-width // slice_) == cluster
 
 
@@ -213,6 +214,41 @@ def test_gather_and_staged_table_agree(stage) -> None:
     want = _oracle(req, table, tokens, **kw)
     out, counts, _ = _explicit(req, table, tokens, cluster=1, stage=stage, prefetch=1, **kw)
     assert np.array_equal(out, want[0]) and np.array_equal(counts, want[1])
+
+
+def _run_fits(width, cluster, chunks):
+    """The explicit geometry's fit rule for a row-wise launch: a CTA's slice
+    (64-column multiples) in runs of 4 x chunks columns over at most 512
+    threads."""
+    slice_ = -(-(-(-width // cluster)) // 64) * 64
+    return -(-slice_ // (4 * chunks)) <= 512
+
+
+@pytest.mark.parametrize("chunks", [1, 2, 4, 8])
+@pytest.mark.parametrize("cluster", [1, 2])
+@pytest.mark.parametrize("width", [1, 7, 31, 32, 33, 100, 255, 1000, 2047, 2048, 2052, 4100, 8192])
+def test_run_lengths(chunks, cluster, width) -> None:
+    """Every run length (4, 8, 16, 32 columns per thread) on whole and split
+    rows, staged and gathered: ragged widths end inside a run, rows of odd
+    width start off the 32-byte and 16-byte boundaries, and the -1 tail
+    starts anywhere."""
+    if not _slices_fit(width, cluster, 0) or not _run_fits(width, cluster, chunks):
+        pytest.skip("geometry does not fit")
+    rng = np.random.default_rng(width * 8 + chunks + 100 * cluster)
+    batch = 7
+    for index, (bs, dcp, rank, il) in enumerate(GEOMETRIES):
+        table_width = int(rng.integers(1, 200))
+        tokens = rng.integers(-3, bs * table_width * dcp + 2 * bs, size=(batch, width), dtype=np.int32)
+        table = rng.integers(-3, 70000, size=(4, table_width), dtype=np.int32)
+        req = rng.integers(0, 4, size=batch, dtype=np.int32)
+        for compact in (True, False):
+            kw = dict(block_size=bs, dcp_size=dcp, dcp_rank=rank, dcp_interleave=il,
+                      compact_valid_to_front=compact)
+            want = _oracle(req, table, tokens, **kw)
+            out, counts, _ = _explicit(req, table, tokens, cluster=cluster, stage=index % 2, prefetch=1,
+                                       chunks=chunks, **kw)
+            assert np.array_equal(out, want[0]), kw
+            assert np.array_equal(counts, want[1]), kw
 
 
 def test_wide_table_is_gathered() -> None:
@@ -513,7 +549,7 @@ def test_decode_step_of_48_layers_in_one_graph(golden) -> None:
 @pytest.mark.parametrize("width", [4, 100, 512, 2048, 6000])
 @pytest.mark.parametrize("batch", [1, 147, 148, 149, 296, 297, 1000, 3000])
 def test_row_groups_over_batch_sizes(width, batch) -> None:
-    """Row-wise CTAs pack several rows (up to 1024 threads) and spread the batch
+    """Row-wise CTAs pack several rows (up to 512 threads) and spread the batch
     over at most one CTA per SM; every batch/width split must stay exact."""
     if batch * width > 4_000_000:
         pytest.skip("large case covered by the full-size tests")
@@ -531,9 +567,10 @@ def test_row_groups_over_batch_sizes(width, batch) -> None:
 
 @pytest.mark.parametrize("batch", [40, 300, 1000])
 def test_staged_table_with_packed_rows_and_mixed_speculation(batch) -> None:
-    """Several rows share a CTA; some rows' request is their own index (the
-    staged copy is right), others' is not (the copy is repaired). Each row
-    synchronises only its own group, so the mix must stay exact."""
+    """Several rows share a CTA as row groups; some rows' request is their own
+    index (the speculatively staged table row is right), others' is not (the
+    copy is repaired), and the groups of one CTA share its barriers, so the
+    mix must stay exact."""
     rng = np.random.default_rng(batch + 99)
     width = 512
     table = rng.integers(-2, 70000, size=(batch + 5, 40), dtype=np.int32)
