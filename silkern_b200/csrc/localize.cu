@@ -731,9 +731,13 @@ int choose_geometry(const Request& r, bool compact, int cluster_req, int stage_r
     g->row_ctas = ctas;
   }
   // Table stage: on request (rows up to kTableStageMax entries), or by
-  // default whenever the row fits and the CTA's shared memory stays modest.
+  // default across a cluster when the row fits and the CTA's shared memory
+  // stays modest. On one CTA the L2 gather measured faster (its latency
+  // hides behind the other warps' issue, while the stage adds instructions);
+  // across a cluster the stage did (the cluster exchange leaves time to
+  // fill it).
   if (stage_req == 1 && r.table_width > kTableStageMax) return SILKERN_E_GEOMETRY;
-  g->stage = stage_req == 1 || (stage_req < 0 && r.table_width <= kTableStageMax);
+  g->stage = stage_req == 1 || (stage_req < 0 && cs > 1 && r.table_width <= kTableStageMax);
   layout_smem(r, compact, g);
   if (stage_req < 0 && g->stage &&
       static_cast<int64_t>(g->smem_group) * 4 * g->rows_per_cta > kStageSmemMax) {
