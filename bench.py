@@ -86,17 +86,34 @@ def _peaks() -> dict:
         return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def _traffic(config: int) -> dict | None:
-    """DRAM bytes per launch from the committed ncu summary of this workload, if any."""
-    name = {"row_stable": "rowwise", "hierarchical_stable": "hierarchical"}[WORKLOADS[config]["arm"]]
-    path = os.path.join(REPO, "profiles", f"localize_{name}_config{config}.md")
+TRAFFIC_FILE = os.path.join(REPO, "profiles", "dram_traffic.json")
+KERNEL_SOURCE = os.path.join(REPO, "silkern_b200", "csrc", "localize.cu")
+
+
+def kernel_digest() -> str:
+    """sha256 of the converter kernel's source, which a traffic capture is tied to."""
+    import hashlib
+
+    with open(KERNEL_SOURCE, "rb") as fh:
+        return hashlib.sha256(fh.read()).hexdigest()
+
+
+def _traffic(config: int) -> dict:
+    """DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)
+    for this workload from the capture data file, when that capture was taken
+    of the current kernel source; otherwise bytes None and the reason."""
     try:
-        with open(path) as fh:
-            text = fh.read()
-    except OSError:
-        return None
-    match = re.search(r"dram_bytes_per_launch:\s*(\d+)", text)
-    return {"bytes": int(match.group(1)), "source": os.path.relpath(path, REPO)} if match else None
+        with open(TRAFFIC_FILE) as fh:
+            data = json.load(fh)
+    except (OSError, ValueError):
+        return {"bytes": None, "source": "no capture data"}
+    entry = data.get("configs", {}).get(str(config))
+    if entry is None:
+        return {"bytes": None, "source": f"no capture of config {config}"}
+    if data.get("kernel_sha256") != kernel_digest():
+        return {"bytes": None, "source": "capture predates the current kernel source"}
+    return {"bytes": int(entry["read"]) + int(entry["write"]), "read": int(entry["read"]),
+            "write": int(entry["write"]), "source": os.path.relpath(TRAFFIC_FILE, REPO)}
 
 
 def _case(config: int, *, seed: int, dcp_rank: int):
@@ -338,41 +355,55 @@ def _reference_hierarchical_direct(ref_silkern, b: dict, g: dict, tile_size: int
 def _replay_seconds(launch, warm_launches: int, timed_launches: int, stream, dev) -> float:
     """Device seconds taken by ``timed_launches`` calls replayed from CUDA graphs.
 
-    ``launch(i)`` issues call ``i``. Calls ``0 .. warm_launches-1`` are captured
-    and replayed untimed first; the timed calls follow them, up to CHUNK calls
-    per graph, replayed back to back on ``stream`` between two CUDA events.
+    ``launch(i)`` issues call ``i``. Calls ``0 .. warm_launches-1`` are the
+    warm-up and the timed calls follow them in the same captured sequence (up
+    to CHUNK calls per graph). The two CUDA events are recorded inside the
+    graphs (external event nodes): the start event on a branch that forks
+    off after the last warm-up call, so it stamps that call's completion
+    without standing between it and the first timed call (which keeps its
+    programmatic dependent launch), and the end event after the last timed
+    call. The timed region therefore holds exactly the timed calls' work in
+    steady state; the latency of launching the first graph is not in it. A
+    ~1 ms device sleep ahead of the replays lets the host queue every graph
+    first.
     """
     import torch
 
-    def plan_graphs(first: int, count: int):
-        graphs = []
-        done = 0
-        while done < count:
-            n = min(CHUNK, count - done)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                for i in range(first + done, first + done + n):
-                    launch(i)
-            graphs.append(graph)
-            done += n
-        return graphs
-
-    warm = plan_graphs(0, warm_launches)
-    timed = plan_graphs(warm_launches, timed_launches)
-    with torch.cuda.stream(stream):
-        for g in warm:
-            g.replay()
+    start = torch.cuda.Event(enable_timing=True, external=True)
+    end = torch.cuda.Event(enable_timing=True, external=True)
+    total = warm_launches + timed_launches
+    graphs = []
+    first = 0
+    side = torch.cuda.Stream(device=dev)
+    while first < total:
+        n = min(CHUNK, total - first)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            forked = False
+            for i in range(first, first + n):
+                if i == warm_launches:
+                    if i > first:  # fork the start stamp off the last warm-up call
+                        side.wait_stream(stream)
+                        start.record(side)
+                        forked = True
+                    else:
+                        start.record(stream)
+                launch(i)
+            if forked:
+                stream.wait_stream(side)
+            if first + n == total:
+                end.record(stream)
+        graphs.append(graph)
+        first += n
     torch.cuda.synchronize(dev)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
-        torch.cuda._sleep(2_000_000)  # ~1 ms: every replay is queued before the start event
-        start.record(stream)
-        for g in timed:
-            g.replay()
-        end.record(stream)
+        torch.cuda._sleep(2_000_000)
+        for graph in graphs:
+            graph.replay()
     torch.cuda.synchronize(dev)
-    return start.elapsed_time(end) / 1e3
+    seconds = start.elapsed_time(end) / 1e3
+    del graphs
+    return seconds
 
 
 def run_triton(args, rank: int, world: int) -> dict | None:
@@ -383,91 +414,33 @@ def run_triton(args, rank: int, world: int) -> dict | None:
     buffer rotation and graph-replay timing as ``run_ours``; outputs are
     checked against the oracle.
     """
-    ref_dir = os.path.join(REPO, "baseline", "_ref")
-    if not os.path.isfile(os.path.join(ref_dir, "silkern", "kernels.py")):
-        return {"impl": "triton-reference", "unavailable": "reference package not installed in baseline/_ref"}
+    ref_silkern = _reference_package()
+    if ref_silkern is None:
+        return {"impl": "triton-reference", "unavailable": "reference package not present in baseline/_ref"}
     if rank != 0:
         return None
-    import numpy as np
     import torch
 
-    import oracle
-
-    sys.path.insert(0, ref_dir)
-    for name in [m for m in sys.modules if m == "silkern" or m.startswith("silkern.")]:
-        del sys.modules[name]
-    import silkern as ref_silkern  # the reference implementation
-
-    if not os.path.abspath(ref_silkern.__file__).startswith(ref_dir):
-        return {"impl": "triton-reference", "unavailable": "could not import the reference package"}
     config = args.config
-    spec = WORKLOADS[config]
-    calls = spec["calls"]
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    distinct = calls if calls > 1 else DISTINCT_CASES
-    cases = [_case(config, seed=1000 + i, dcp_rank=0) for i in range(distinct)]
-    direct = spec["arm"] == "hierarchical_stable" and (
-        cases[0].width > ref_silkern.MAX_ROW_WIDTH or cases[0].tile_size not in ref_silkern.SUPPORTED_TILE_SIZES)
-    bytes_per_call = cases[0].algorithmic_bytes()
-    n_sets = max(64, math.ceil(2.05 * L2_BYTES / bytes_per_call))
-    n_sets = math.ceil(n_sets / distinct) * distinct
-    sets = []
-    for i in range(n_sets):
-        case = cases[i % distinct]
-        bufs = {name: torch.as_tensor(a).to(dev) for name, a in
-                (("req", case.req_ids), ("table", case.block_table), ("tokens", case.tokens))}
-        bufs["out"] = torch.empty_like(bufs["tokens"])
-        bufs["counts"] = torch.empty(case.batch, dtype=torch.int32, device=dev)
-        geometry = case.geometry()
-        if spec["arm"] == "row_stable":
-            call = (lambda b=bufs, g=geometry: ref_silkern.localize_rowwise(
-                b["req"], b["table"], b["tokens"], b["out"], b["counts"], **g))
-        else:
-            tiles = (case.width + case.tile_size - 1) // case.tile_size
-            for name, shape in (("mapped", (case.batch, case.width)), ("local_positions", (case.batch, case.width)),
-                                ("tile_counts", (case.batch, tiles)), ("tile_offsets", (case.batch, tiles))):
-                bufs[name] = torch.empty(shape, dtype=torch.int32, device=dev)
-            if direct:
-                # The reference launcher rejects this width/tile (its workspace
-                # limits), so its four Triton kernels are launched directly with
-                # the launcher's own parameters.
-                call = (lambda b=bufs, g=geometry, t=case.tile_size: _reference_hierarchical_direct(
-                    ref_silkern, b, g, t))
-            else:
-                call = (lambda b=bufs, g=geometry, t=case.tile_size: ref_silkern.localize_hierarchical(
-                    b["req"], b["table"], b["tokens"], b["out"], b["counts"], b["mapped"],
-                    b["local_positions"], b["tile_counts"], b["tile_offsets"], tile_size=t, **g))
-        sets.append((bufs, call))
-    stream = torch.cuda.Stream(device=dev)
-    stream.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(stream):
-        for i in range(n_sets):
-            sets[i][1]()
-    torch.cuda.synchronize(dev)
-    per_step_s = _replay_seconds(lambda i: sets[i % n_sets][1](), args.warmup * calls,
-                                 args.steps * calls, stream, dev) / args.steps
-    per_call_s = per_step_s / calls
-    expected = [oracle.localize(c.req_ids, c.block_table, c.tokens, threads=4, **c.geometry()) for c in cases]
-    bit_exact = all(
-        np.array_equal(sets[i][0]["out"].cpu().numpy(), expected[i % distinct][0])
-        and np.array_equal(sets[i][0]["counts"].cpu().numpy(), expected[i % distinct][1])
-        for i in range(n_sets))
+    sets = ConverterSets(config, shard_plan(0, 1, config), dev, impl="triton", ref_silkern=ref_silkern)
+    t = measure_converter(sets, args.steps, args.warmup, dev)
     peaks = _peaks()
-    achieved = bytes_per_call / per_call_s / 1e9
+    achieved = sets.bytes_per_call / t["per_call_s"] / 1e9
     return {
         "impl": "triton-reference",
         "metric": METRIC if config == 3 else f"Gindices/s per B200, config {config}",
-        "value": calls * cases[0].batch * cases[0].width / per_step_s / 1e9,
+        "value": sets.calls * sets.indices_per_call / t["per_step_s"] / 1e9,
         "unit": UNIT,
         "n_gpus": 1,
         "steps": args.steps,
         "warmup": args.warmup,
-        "us_per_call": per_call_s * 1e6,
-        "bit_exact": bit_exact,
+        "us_per_call": t["per_call_s"] * 1e6,
+        "bit_exact": t["bit_exact"],
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"]},
-        "config": _workload_config(config, 1, n_sets),
+        "config": _workload_config(config, 1, sets.n_sets),
         "source": "reference silkern.localize_rowwise / localize_hierarchical (Triton) from baseline/_ref",
     }
 
@@ -795,128 +768,249 @@ def _make_call(arm: str, bufs: dict, geometry: dict, tile_size: int):
         **geometry)
 
 
-def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
-    import numpy as np
+def _reference_package():
+    """The reference's own silkern package from baseline/_ref, or None."""
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref_dir, "silkern", "kernels.py")):
+        return None
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    for name in [m for m in sys.modules if m == "silkern" or m.startswith("silkern.")]:
+        del sys.modules[name]
+    import silkern as ref_silkern  # the reference implementation
+
+    if not os.path.abspath(ref_silkern.__file__).startswith(ref_dir):
+        return None
+    return ref_silkern
+
+
+def _reference_call(ref_silkern, arm: str, bufs: dict, case):
+    """The reference's own launcher (Triton) for one buffer set."""
+    g = case.geometry()
+    if arm == "row_stable":
+        return lambda: ref_silkern.localize_rowwise(bufs["req"], bufs["table"], bufs["tokens"], bufs["out"],
+                                                    bufs["counts"], **g)
+    if case.width > ref_silkern.MAX_ROW_WIDTH or case.tile_size not in ref_silkern.SUPPORTED_TILE_SIZES:
+        # The reference launcher rejects this width/tile (its workspace
+        # limits), so its four Triton kernels are launched directly with the
+        # launcher's own parameters.
+        return lambda: _reference_hierarchical_direct(ref_silkern, bufs, g, case.tile_size)
+    return lambda: ref_silkern.localize_hierarchical(
+        bufs["req"], bufs["table"], bufs["tokens"], bufs["out"], bufs["counts"], bufs["mapped"],
+        bufs["local_positions"], bufs["tile_counts"], bufs["tile_offsets"], tile_size=case.tile_size, **g)
+
+
+class ConverterSets:
+    """Resident buffer sets for one workload, each with its converter call.
+
+    Inputs rotate over enough sets to exceed 2.05 x L2 (126 MB), so every
+    timed call reads data that is not already in L2. ``impl`` is "ours" (the
+    public launchers), "atomic" (the comparison baseline) or "triton" (the
+    reference's own launchers, ``ref_silkern``).
+    """
+
+    def __init__(self, config: int, plan: dict, dev, *, impl: str = "ours", rows: int = 0,
+                 ref_silkern=None, min_sets: int = 64):
+        import torch
+
+        from silkern_b200.workspace import workspace_shapes
+
+        spec = WORKLOADS[config]
+        self.config = config
+        self.arm = spec["arm"]
+        self.calls = spec["calls"]
+        distinct = self.calls if self.calls > 1 else DISTINCT_CASES
+        if rows > 0:  # fewer, larger cases: every call's rows repeat a config case's
+            distinct = self.calls if self.calls > 1 else 2
+        cases = [_case(config, seed=plan["base_seed"] + i, dcp_rank=plan["dcp_rank"]) for i in range(distinct)]
+        if rows > 0:
+            cases = [_stack_rows(c, rows) for c in cases]
+        self.cases = cases
+        self.distinct = distinct
+        self.bytes_per_call = cases[0].algorithmic_bytes()
+        self.indices_per_call = cases[0].batch * cases[0].width
+        n_sets = max(min_sets if rows == 0 else 2, math.ceil(2.05 * L2_BYTES / self.bytes_per_call))
+        self.n_sets = math.ceil(n_sets / distinct) * distinct
+        self.impl = impl
+        self.sets = []
+        for i in range(self.n_sets):
+            case = cases[i % distinct]
+            bufs = {name: torch.as_tensor(a).to(dev) for name, a in
+                    (("req", case.req_ids), ("table", case.block_table), ("tokens", case.tokens))}
+            bufs["out"] = torch.empty_like(bufs["tokens"])
+            bufs["counts"] = torch.empty(case.batch, dtype=torch.int32, device=dev)
+            if self.arm == "hierarchical_stable":
+                for name, shape in workspace_shapes(case.batch, case.width, tile_size=case.tile_size).items():
+                    bufs[name] = torch.empty(shape, dtype=torch.int32, device=dev)
+            if impl == "atomic":
+                bufs["scratch"] = torch.empty(case.batch, dtype=torch.int32, device=dev)
+            if impl == "triton":
+                call = _reference_call(ref_silkern, self.arm, bufs, case)
+            else:
+                call = _make_call("atomic" if impl == "atomic" else self.arm, bufs, case.geometry(),
+                                  case.tile_size)
+            self.sets.append((bufs, call))
+
+    def launch(self, i: int) -> None:
+        self.sets[i % self.n_sets][1]()
+
+    def bit_exact(self, used) -> bool:
+        """Every used set's out and counts equal the oracle's (for the atomic
+        baseline: the same set and counts, in any order)."""
+        import numpy as np
+
+        import oracle
+
+        expected = [oracle.localize(c.req_ids, c.block_table, c.tokens, threads=4, **c.geometry())
+                    for c in self.cases]
+        ok = True
+        for index in sorted(used):
+            bufs = self.sets[index][0]
+            want_out, want_counts = expected[index % self.distinct]
+            got_out = bufs["out"].cpu().numpy()
+            if self.impl == "atomic":
+                big = np.iinfo(np.int32).max
+                got_out = np.sort(np.where(got_out < 0, big, got_out), axis=1)
+                want_out = np.sort(np.where(want_out < 0, big, want_out), axis=1)
+            if not (np.array_equal(got_out, want_out)
+                    and np.array_equal(bufs["counts"].cpu().numpy(), want_counts)):
+                ok = False
+        return ok
+
+
+def _all_ranks(dist, ok: bool) -> bool:
+    """True when ``ok`` holds on every rank."""
+    return reduce_max(dist, 0.0 if ok else 1.0) == 0.0
+
+
+def measure_converter(sets: ConverterSets, steps: int, warmup: int, dev, dist=None, sampler=None) -> dict:
+    """Time ``steps`` steps after ``warmup`` (CUDA events inside the replayed
+    graphs, max over ranks, a barrier and a synchronize on both sides) and
+    check every used buffer set against the oracle."""
+    import contextlib
+
     import torch
-
-    import oracle
-    from silkern_b200 import _native
-    from silkern_b200.workspace import workspace_shapes
-
-    config = args.config
-    spec = dict(WORKLOADS[config])
-    if args.impl == "atomic":
-        spec["arm"] = "atomic"
-    calls = spec["calls"]
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    plan = shard_plan(rank, world, config)
-
-    distinct = calls if calls > 1 else DISTINCT_CASES
-    if args.rows > 0:  # fewer, larger cases: every call's rows repeat a config case's
-        distinct = calls if calls > 1 else 2
-    cases = [_case(config, seed=plan["base_seed"] + i, dcp_rank=plan["dcp_rank"]) for i in range(distinct)]
-    if args.rows > 0:
-        cases = [_stack_rows(c, args.rows) for c in cases]
-    bytes_per_call = cases[0].algorithmic_bytes()
-    n_sets = max(64 if args.rows == 0 else 2, math.ceil(2.05 * L2_BYTES / bytes_per_call))
-    n_sets = math.ceil(n_sets / distinct) * distinct
-    sets = []
-    for i in range(n_sets):
-        case = cases[i % distinct]
-        bufs = {name: torch.as_tensor(a).to(dev) for name, a in
-                (("req", case.req_ids), ("table", case.block_table), ("tokens", case.tokens))}
-        bufs["out"] = torch.empty_like(bufs["tokens"])
-        bufs["counts"] = torch.empty(case.batch, dtype=torch.int32, device=dev)
-        if spec["arm"] == "hierarchical_stable":
-            for name, shape in workspace_shapes(case.batch, case.width, tile_size=case.tile_size).items():
-                bufs[name] = torch.empty(shape, dtype=torch.int32, device=dev)
-        if spec["arm"] == "atomic":
-            bufs["scratch"] = torch.empty(case.batch, dtype=torch.int32, device=dev)
-        sets.append((bufs, _make_call(spec["arm"], bufs, case.geometry(), case.tile_size)))
-    indices_per_call = cases[0].batch * cases[0].width
-
-    def launch(i: int) -> None:
-        sets[i % n_sets][1]()
 
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(stream):
-        for i in range(max(3, n_sets)):
-            launch(i)
+        for i in range(max(3, sets.n_sets)):
+            sets.launch(i)
     torch.cuda.synchronize(dev)
-
-    def plan_graphs(first: int, count: int):
-        graphs = []
-        done = 0
-        while done < count:
-            n = min(CHUNK, count - done)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                for i in range(first + done, first + done + n):
-                    launch(i)
-            graphs.append(graph)
-            done += n
-        return graphs
-
-    warm_launches = args.warmup * calls
-    timed_launches = args.steps * calls
-    warm_graphs = plan_graphs(0, warm_launches)
-    main_graphs = plan_graphs(warm_launches, timed_launches)
-    torch.cuda.synchronize(dev)
-    with torch.cuda.stream(stream):
-        for g in warm_graphs:
-            g.replay()
-    torch.cuda.synchronize(dev)
-
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
+    warm_launches = warmup * sets.calls
+    timed_launches = steps * sets.calls
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
+    with sampler if sampler is not None else contextlib.nullcontext():
+        seconds = _replay_seconds(sets.launch, warm_launches, timed_launches, stream, dev)
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    per_step_s = reduce_max(dist, seconds) / steps
+    used = {i % sets.n_sets for i in range(max(3, sets.n_sets) + warm_launches + timed_launches)}
+    ok = _all_ranks(dist, sets.bit_exact(used))
+    return {"per_step_s": per_step_s, "per_call_s": per_step_s / sets.calls, "bit_exact": ok}
+
+
+def measure_isolated(sets: ConverterSets, steps: int, warmup: int, dev) -> float:
+    """Seconds one converter call adds between a producer kernel that writes
+    its tokens and a consumer kernel that reads its output, with no other
+    converter call around it: [producer, converter, consumer] per step,
+    minus [producer, consumer] per step, over rotating sets. Programmatic
+    dependent launch cannot overlap the call with a previous converter call
+    here, so this is the latency of one call in a pipeline."""
+    import torch
+
+    sources = [b["tokens"].clone() for b, _ in sets.sets]
+    sinks = [torch.empty_like(b["out"]) for b, _ in sets.sets]
+
+    def with_call(i: int) -> None:
+        k = i % sets.n_sets
+        bufs, call = sets.sets[k]
+        bufs["tokens"].copy_(sources[k])  # producer: writes the converter's input
+        call()
+        sinks[k].copy_(bufs["out"])  # consumer: reads the converter's output
+
+    def without_call(i: int) -> None:
+        k = i % sets.n_sets
+        bufs, _ = sets.sets[k]
+        bufs["tokens"].copy_(sources[k])
+        sinks[k].copy_(bufs["out"])
+
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    warm = max(3, warmup) * sets.calls
+    timed = steps * sets.calls
+    t_with = _replay_seconds(with_call, warm, timed, stream, dev)
+    t_without = _replay_seconds(without_call, warm, timed, stream, dev)
+    return (t_with - t_without) / timed
+
+
+def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
+    import torch
+
+    from silkern_b200 import _native
+
+    config = args.config
+    impl = "atomic" if args.impl == "atomic" else "ours"
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    plan = shard_plan(rank, world, config)
+    sets = ConverterSets(config, plan, dev, impl=impl, rows=args.rows)
+    calls = sets.calls
     sampler = ClockSampler(local_rank)
-    with sampler:
-        with torch.cuda.stream(stream):
-            torch.cuda._sleep(2_000_000)  # ~1 ms: every replay is queued before the start event
-            start.record(stream)
-            for g in main_graphs:
-                g.replay()
-            end.record(stream)
-        torch.cuda.synchronize(dev)
-    if dist is not None:
-        dist.barrier()
-    elapsed_ms = reduce_max(dist, start.elapsed_time(end))
-    per_step_s = elapsed_ms / 1e3 / args.steps
-    per_call_s = per_step_s / calls
+    timing = measure_converter(sets, args.steps, args.warmup, dev, dist, sampler)
+    per_step_s, per_call_s = timing["per_step_s"], timing["per_call_s"]
+    bytes_per_call = sets.bytes_per_call
+    indices_per_call = sets.indices_per_call
+    n_sets = sets.n_sets
+    headline_cases = sets.cases[:calls]
 
-    # The timed outputs must be the reference's: check every buffer set used.
-    expected = [oracle.localize(c.req_ids, c.block_table, c.tokens, threads=4, **c.geometry())
-                for c in cases]
-    used = {i % n_sets for i in range(warm_launches + timed_launches)}
-    bit_exact = True
-    for index in sorted(used):
-        bufs = sets[index][0]
-        want_out, want_counts = expected[index % distinct]
-        got_out = bufs["out"].cpu().numpy()
-        if spec["arm"] == "atomic":  # same set and count; the order is unspecified
-            got_out = np.sort(np.where(got_out < 0, np.iinfo(np.int32).max, got_out), axis=1)
-            want_out = np.sort(np.where(want_out < 0, np.iinfo(np.int32).max, want_out), axis=1)
-        if not (np.array_equal(got_out, want_out)
-                and np.array_equal(bufs["counts"].cpu().numpy(), want_counts)):
-            bit_exact = False
-    del warm_graphs, main_graphs
+    isolated = None
+    if impl == "ours" and world == 1 and args.rows == 0:
+        isolated = measure_isolated(sets, min(args.steps, 200), args.warmup, dev)
+    del sets
+    torch.cuda.empty_cache()
 
-    e2e = run_e2e(args, cases[:calls], dev, dist) if args.impl == "ours" else None
+    extra = {}
+    if impl == "ours" and args.rows == 0 and not args.headline_only:
+        # The other workloads, timed the same way on this GPU's DCP rank.
+        others = {}
+        for other in sorted(WORKLOADS):
+            if other == config:
+                continue
+            other_plan = shard_plan(rank, world, other)
+            other_sets = ConverterSets(other, other_plan, dev)
+            t = measure_converter(other_sets, args.steps, args.warmup, dev, dist)
+            others[str(other)] = {
+                "workload": WORKLOADS[other]["desc"],
+                "us_per_call": t["per_call_s"] * 1e6,
+                "value": world * other_sets.calls * other_sets.indices_per_call / t["per_step_s"] / 1e9,
+                "unit": UNIT,
+                "bit_exact": t["bit_exact"],
+                "dcp_rank": f"gpu_index % {WORKLOADS[other]['dcp_size']}",
+                "frac": other_sets.bytes_per_call / t["per_call_s"] / 1e9 / _peaks()["hbm_gbs"],
+            }
+            del other_sets
+            torch.cuda.empty_cache()
+        extra["configs"] = others
+        if world == 1:
+            extra["triton_reference"] = _triton_sub(config, args, dev)
+        extra["replay_gate"] = _replay_gate_sub(rank, world, dev, dist)
+
+    e2e = run_e2e(args, headline_cases, dev, dist) if impl == "ours" else None
 
     peaks = _peaks()
     achieved = bytes_per_call / per_call_s / 1e9
-    traffic = _traffic(config) if args.rows == 0 else None  # the committed capture is of the default rows
+    traffic = _traffic(config) if args.rows == 0 else {"bytes": None, "source": "captures are of the default rows"}
     workload = _workload_config(config, world, n_sets)
     if args.rows > 0:
         workload["rows_per_call"] = args.rows
         workload["workload"] += f"; {args.rows} rows per call, the config's rows repeated"
+    frac = achieved / peaks["hbm_gbs"]
     result = {
-        **({"impl": "atomic-baseline"} if args.impl == "atomic" else {}),
+        **({"impl": "atomic-baseline"} if impl == "atomic" else {}),
         "metric": METRIC if config == 3 else f"Gindices/s per B200, config {config}",
         "value": world * calls * indices_per_call / per_step_s / 1e9,
         "unit": UNIT,
@@ -931,21 +1025,26 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
         "dtype": "int32",
         "data": f"synthetic (seeded; config {config} shapes)",
         "config": workload,
-        "bit_exact": bit_exact,
+        "bit_exact": timing["bit_exact"],
         "hbm_gbs": achieved,
         "roofline": {
             "bound": "hbm",
             "achieved": achieved,
             "peak": peaks["hbm_gbs"],
             "unit": "GB/s",
-            "frac": achieved / peaks["hbm_gbs"],
-            "traffic": traffic["bytes"] if traffic else None,
-            "traffic_source": traffic["source"] if traffic else None,
+            "frac": frac,
+            "traffic": traffic["bytes"],
+            "traffic_source": traffic["source"],
+            "dram_gbs": None if traffic["bytes"] is None else traffic["bytes"] / per_call_s / 1e9,
             "algorithmic_bytes_per_call": bytes_per_call,
             "peak_source": peaks["source"],
-            "timing": "CUDA events around the graph replays of the timed calls, per call",
+            "regime": "bandwidth" if frac >= 0.6 else
+                      "latency and issue: one call moves too few bytes to fill HBM, see us_per_call",
+            "timing": "CUDA events recorded inside the replayed graphs around the timed calls, per call",
         },
-        "gpu_launches": timed_launches,
+        "isolated_us_per_call": None if isolated is None else isolated * 1e6,
+        "gpu_launches": args.steps * calls,
+        **extra,
         "e2e": e2e,
         "clocks": sampler.summary(),
         "library": _native.LIB_PATH,
@@ -953,6 +1052,57 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = _cpu_baseline(config, _host_threads())
     return result if rank == 0 else None
+
+
+def _replay_gate_sub(rank: int, world: int, dev, dist) -> dict:
+    """Config 5's decode step on this GPU's DCP rank: 48 converter calls of
+    128 x 2048 (dcp 8), each layer on its own seeded selection, captured once
+    and replayed 10,000 times, every layer of every replay compared with the
+    oracle on the device; pointers and the allocator checked at replay 0, 1,
+    10, 100, 1000 and 10000. Every rank runs it; the line reports all ranks."""
+    import oracle
+    from silkern_b200.verify import GATE_REPLAYS, decode_step_gate
+
+    plan = shard_plan(rank, world, 5)
+    layers = [_case(5, seed=plan["base_seed"] + 7000 + layer, dcp_rank=plan["dcp_rank"])
+              for layer in range(WORKLOADS[5]["calls"])]
+    expected = [oracle.localize(c.req_ids, c.block_table, c.tokens, threads=4, **c.geometry()) for c in layers]
+    gate = decode_step_gate(layers, expected=expected, replays=GATE_REPLAYS)
+    return {
+        "workload": WORKLOADS[5]["desc"],
+        "layers": len(layers),
+        "replays": int(reduce_max(dist, -gate.replays)) * -1,  # the fewest over ranks
+        "mismatches": int(reduce_max(dist, max(gate.mismatches, 0) if gate.error is None else 1 << 30)),
+        "checkpoints": sorted(gate.checkpoints),
+        "ok": _all_ranks(dist, gate.ok),
+        "converter_step_us": reduce_max(dist, gate.step_us or 0.0),
+        "dcp_rank": "gpu_index % 8",
+        "error": gate.error,
+    }
+
+
+def _triton_sub(config: int, args, dev) -> dict:
+    """The reference's own Triton launcher on the same workload, same
+    rotation and timing, in this process (a comparison beside the headline)."""
+    import torch
+
+    ref_silkern = _reference_package()
+    if ref_silkern is None:
+        return {"unavailable": "reference package not present in baseline/_ref"}
+    try:
+        sets = ConverterSets(config, shard_plan(0, 1, config), dev, impl="triton", ref_silkern=ref_silkern)
+        t = measure_converter(sets, args.steps, args.warmup, dev)
+        isolated = measure_isolated(sets, min(args.steps, 200), args.warmup, dev)
+    except Exception as exc:  # the comparison arm must not take the headline down
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+    finally:
+        torch.cuda.empty_cache()
+    return {
+        "us_per_call": t["per_call_s"] * 1e6,
+        "isolated_us_per_call": isolated * 1e6,
+        "bit_exact": t["bit_exact"],
+        "source": "reference silkern.localize_rowwise / localize_hierarchical (Triton) from baseline/_ref",
+    }
 
 
 def _stack_rows(case, rows: int):
@@ -1077,6 +1227,26 @@ def run_e2e(args, cases, dev, dist) -> dict:
 
     captured = timed(replay)
     del graphs
+    # The host link's ceiling: the same captured copies on the same lanes and
+    # buffers, without the converter call.
+    link_graphs = []
+    for lane_index, (stream, jobs) in enumerate(lanes):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for host_in, dev_in, bufs, host_out, host_counts, _ in jobs:
+                dev_in.copy_(host_in, non_blocking=True)
+                host_out.copy_(bufs["out"], non_blocking=True)
+                host_counts.copy_(bufs["counts"], non_blocking=True)
+        link_graphs.append(graph)
+    torch.cuda.synchronize(dev)
+
+    def replay_link(i: int) -> None:
+        stream, _ = lanes[i % n_lanes]
+        with torch.cuda.stream(stream):
+            link_graphs[i % n_lanes].replay()
+
+    link = timed(replay_link)
+    del link_graphs
     world = dist.get_world_size() if dist is not None else 1
     indices = len(cases) * cases[0].batch * cases[0].width
     return {
@@ -1090,6 +1260,8 @@ def run_e2e(args, cases, dev, dist) -> dict:
                 f"stream (CUDA graph) and replayed on {n_lanes} alternating streams, pinned host buffers",
         "eager_us_per_step": eager * 1e6,
         "eager_value": world * indices / eager / 1e9,
+        "link_us_per_step": link * 1e6,
+        "link_gbs_per_gpu": (h2d + d2h) / link / 1e9,
     }
 
 
@@ -1108,6 +1280,8 @@ def main(argv=None) -> int:
                         help="rows per converter call: the workload's rows repeated (default: its own batch)")
     parser.add_argument("--e2e-lanes", type=int, default=4,
                         help="streams the end-to-end steps alternate over, each with its own buffers")
+    parser.add_argument("--headline-only", action="store_true",
+                        help="skip the other workloads, the Triton comparison and the replay gate")
     args = parser.parse_args(argv)
     if args.steps < 1 or args.warmup < 0:
         parser.error("--steps must be >= 1 and --warmup >= 0")

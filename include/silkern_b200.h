@@ -175,6 +175,16 @@ int silkern_count_mismatches_v1(const int32_t* a, const int32_t* b, int64_t n,
                                 int32_t* mismatches, void* stream);
 
 /*
+ * silkern_count_mismatches_v1 per segment, for the decode-step replay gate:
+ * a and b hold `segments` consecutive segments of segment_elems int32 each
+ * (one per layer of a step), and counters[s] (int32, segments entries) is
+ * increased by the number of positions of segment s where a and b differ.
+ * One launch; segments <= 65535. No counterpart in the reference.
+ */
+int silkern_count_segment_mismatches_v1(const int32_t* a, const int32_t* b, int64_t segments,
+                                        int64_t segment_elems, int32_t* counters, void* stream);
+
+/*
  * Comparison baseline, not the product: the atomic-reservation converter of
  * the reference's bench/atomic_baseline.py:40-111 and :313-385 (itself a
  * restatement of the upstream vLLM converter). Same set and counts as the

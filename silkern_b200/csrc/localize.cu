@@ -468,6 +468,30 @@ __global__ void __launch_bounds__(256) count_mismatches_kernel(const int32_t* a,
   }
 }
 
+// counters[s] += the number of differing positions inside segment s of
+// segment_elems elements; blockIdx.y is the segment.
+__global__ void __launch_bounds__(256) count_segment_mismatches_kernel(const int32_t* a, const int32_t* b,
+                                                                       int64_t segment_elems,
+                                                                       int32_t* counters) {
+  __shared__ int s_part[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t base = static_cast<int64_t>(blockIdx.y) * segment_elems;
+  int local = 0;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < segment_elems; i += stride) {
+    local += a[base + i] != b[base + i] ? 1 : 0;
+  }
+  local = __reduce_add_sync(kFull, local);
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = local;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int total = 0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) total += s_part[w];
+    if (total != 0) atomicAdd(counters + blockIdx.y, total);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -1090,6 +1114,33 @@ extern "C" int silkern_count_mismatches_v1(const int32_t* a, const int32_t* b, i
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, silkern::count_mismatches_kernel, a, b, n, mismatches);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -static_cast<int>(err);
+  }
+  return SILKERN_OK;
+}
+
+extern "C" int silkern_count_segment_mismatches_v1(const int32_t* a, const int32_t* b, int64_t segments,
+                                                   int64_t segment_elems, int32_t* counters,
+                                                   void* stream) {
+  if (!a || !b || !counters) return SILKERN_E_NULL;
+  if (segments < 0 || segments > 65535 || segment_elems < 0) return SILKERN_E_SHAPE;
+  if (segments == 0 || segment_elems == 0) return SILKERN_OK;
+  int64_t blocks = (segment_elems + 255) / 256;
+  const int64_t cap = (static_cast<int64_t>(silkern::sm_count()) * 8 + segments - 1) / segments;
+  if (blocks > cap) blocks = cap;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(segments), 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, silkern::count_segment_mismatches_kernel, a, b,
+                                             segment_elems, counters);
   if (err != cudaSuccess) {
     (void)cudaGetLastError();
     return -static_cast<int>(err);

@@ -345,3 +345,25 @@ def count_mismatches(a, b, mismatches) -> None:
             a.data_ptr(), b.data_ptr(), a.numel(), mismatches.data_ptr(), stream
         )
     _native.check(code, "count_mismatches")
+
+
+def count_segment_mismatches(a, b, counters) -> None:
+    """``counters[s] +=`` the number of differing elements in segment ``s``,
+    where segment ``s`` is ``a[s]`` against ``b[s]`` (int32 tensors of one
+    shape, first dimension = segments). One launch; capturable in a CUDA graph.
+    """
+    import torch
+
+    if a.shape != b.shape or a.dtype != torch.int32 or b.dtype != torch.int32 or a.dim() < 1:
+        raise LocalizationError("count_segment_mismatches needs two int32 tensors of one shape")
+    if not (a.is_contiguous() and b.is_contiguous()) or counters.numel() < a.shape[0]:
+        raise LocalizationError("count_segment_mismatches needs contiguous inputs and one counter per segment")
+    lib = _native.load()
+    segments = a.shape[0]
+    with _device_scope(torch, a.device):
+        stream = torch.cuda.current_stream(a.device).cuda_stream
+        code = lib.silkern_count_segment_mismatches_v1(
+            a.data_ptr(), b.data_ptr(), segments, a.numel() // max(segments, 1), counters.data_ptr(), stream
+        )
+    _native.check(code, "count_segment_mismatches")
+

@@ -5,8 +5,9 @@
     >>> report.ok                               # doctest: +SKIP
     True
 
-Interface and checks of silkern/verify.py:389-447. Each (arm, geometry) cell
-runs five checks:
+The interface follows the reference's silkern/verify.py:389-447: a matrix of
+geometries, each run through both arms, each (arm, geometry) cell judged by
+five named checks (:data:`CHECKS`):
 
 ``oracle``        output and counts equal :func:`localize_reference` elementwise;
 ``order``         the valid prefix equals the input row filtered by ownership and
@@ -15,27 +16,43 @@ runs five checks:
 ``replay``        the launch captured in a CUDA graph and replayed keeps every
                   pointer and ``torch.cuda.memory_allocated()`` unchanged and
                   still produces the oracle's output;
-``immutability``  inputs are unchanged and the guard elements around every
-                  output and workspace buffer are still zero.
+``immutability``  inputs are unchanged and the sentinel guards around every
+                  output and workspace buffer are untouched.
 
-:func:`replay_gate` adds the long-run check: a graph holding
-(poison out, localize, device-side compare with the expected result) is
-replayed 10,000 times; every replay is checked for bit-exactness through a
-preallocated mismatch counter, and pointers plus the allocator are checked at
-replay 0, 1, 10, 100, 1000 and 10000.
+Here a cell is a :class:`_Fixture` (the case, its device buffers inside
+sentinel guards, and the expected result, built once) and each check is a
+function of the fixture, registered in :data:`_CHECK_FUNCTIONS`; the runner
+applies the registry in order and records a failure instead of raising.
 
-A failing cell is reported, not raised.
+Two long-run gates go beyond the reference (whose replay check is 32 replays,
+silkern/verify.py:352-372):
+
+* :func:`replay_gate` replays one captured call 10,000 times;
+* :func:`decode_step_gate` replays a whole captured decode step, one
+  converter call per layer on its own inputs (48 layers of 128 x 2048 by
+  default), 10,000 times.
+
+Both poison the outputs before every replay and compare them with the
+expected result on the device, into preallocated mismatch counters (one per
+layer for the step), so every replay is checked; pointers, allocated and
+reserved memory are compared with their values after capture at replay 0, 1,
+10, 100, 1000 and 10000.
 """
 
 from __future__ import annotations
 
 import random
-from collections.abc import Sequence
+from collections.abc import Callable, Sequence
 from dataclasses import dataclass, field
 
 from silkern_b200.contract import DEFAULT_TILE_SIZE, MAX_ROW_WIDTH, localize_reference
 from silkern_b200.errors import LocalizationError
-from silkern_b200.kernels import count_mismatches, localize_hierarchical, localize_rowwise
+from silkern_b200.kernels import (
+    count_mismatches,
+    count_segment_mismatches,
+    localize_hierarchical,
+    localize_rowwise,
+)
 from silkern_b200.workspace import workspace_shapes
 
 CHECKS = ("oracle", "order", "determinism", "replay", "immutability")
@@ -65,11 +82,13 @@ DETERMINISM_REPEATS = 8
 GATE_REPLAYS = 10_000
 GATE_CHECKPOINTS = (0, 1, 10, 100, 1000, 10_000)
 POISON = 0x5A5A5A5A
+_GEOMETRY_KEYS = ("block_size", "dcp_size", "dcp_rank", "dcp_interleave")
 
 
 @dataclass
 class CellReport:
-    """Outcome of one (arm, geometry) cell."""
+    """Outcome of one (arm, geometry) cell: one boolean per check, or the
+    exception text when the cell could not run."""
 
     arm: str
     geometry: dict[str, int]
@@ -81,14 +100,16 @@ class CellReport:
         return self.error is None and all(self.checks.values())
 
     def failures(self) -> list[str]:
+        """The failed checks by name (or the error), empty when the cell passed."""
         if self.error is not None:
             return [f"error: {self.error}"]
-        return [name for name, passed in self.checks.items() if not passed]
+        return [name for name in self.checks if not self.checks[name]]
 
 
 @dataclass
 class ConformanceReport:
-    """Aggregate outcome; truthy iff every cell passed every check."""
+    """Every cell's outcome; truthy exactly when at least one cell ran and
+    every cell passed every check."""
 
     cells: list[CellReport] = field(default_factory=list)
     device: str = "unknown"
@@ -96,32 +117,34 @@ class ConformanceReport:
 
     @property
     def ok(self) -> bool:
-        return self.skipped is None and bool(self.cells) and all(c.ok for c in self.cells)
+        if self.skipped is not None or not self.cells:
+            return False
+        return not any(self.failed())
 
     def __bool__(self) -> bool:
         return self.ok
 
+    def failed(self) -> list[CellReport]:
+        return [cell for cell in self.cells if not cell.ok]
+
     def summary(self) -> str:
         if self.skipped is not None:
             return f"conformance skipped: {self.skipped}"
-        passed = sum(1 for c in self.cells if c.ok)
-        head = (
-            f"silkern_b200 conformance on {self.device}: "
-            f"{passed}/{len(self.cells)} cells passed ({', '.join(CHECKS)})"
-        )
-        if passed == len(self.cells):
-            return head
-        lines = [head, ""]
-        for cell in self.cells:
-            if cell.ok:
-                continue
-            geometry = " ".join(f"{k}={v}" for k, v in cell.geometry.items())
-            lines.append(f"  FAIL {cell.arm:22s} {geometry}")
-            lines.extend(f"       - {failure}" for failure in cell.failures())
+        failed = self.failed()
+        lines = [f"silkern_b200 conformance on {self.device}: "
+                 f"{len(self.cells) - len(failed)}/{len(self.cells)} cells passed ({', '.join(CHECKS)})"]
+        if failed:
+            lines.append("")
+            lines += [_failure_lines(cell) for cell in failed]
         return "\n".join(lines)
 
     def __str__(self) -> str:  # pragma: no cover - convenience
         return self.summary()
+
+
+def _failure_lines(cell: CellReport) -> str:
+    where = " ".join(f"{key}={value}" for key, value in cell.geometry.items())
+    return "\n".join([f"  FAIL {cell.arm:22s} {where}"] + [f"       - {f}" for f in cell.failures()])
 
 
 def _random_case(
@@ -132,7 +155,8 @@ def _random_case(
     dcp_size: int,
     seed: int,
 ) -> tuple[list[int], list[list[int]], list[list[int]]]:
-    """One adversarial case (same mix as silkern/verify.py:132-170).
+    """One adversarial case, drawn in the order of silkern/verify.py:132-170
+    so that a recorded seed reproduces the reference's own inputs.
 
     About 12% negative tokens, 8% tokens just past the end of the page table,
     a fragmented page table with negative entries, four requests shared by the
@@ -193,151 +217,142 @@ def _expected_order(
     return kept
 
 
-def _guarded(torch, shape, device):
-    """A zero-guarded int32 tensor: returns ``(view, backing storage)``."""
-    total = 1
-    for dim in shape:
-        total *= dim
-    storage = torch.zeros(total + 2 * GUARD_ELEMENTS, dtype=torch.int32, device=device)
-    return storage[GUARD_ELEMENTS : GUARD_ELEMENTS + total].view(*shape), storage
+class _Guarded:
+    """An int32 device buffer with POISON sentinels on both sides, so a write
+    out of bounds in either direction is visible afterwards."""
+
+    def __init__(self, torch, shape, device):
+        elements = 1
+        for extent in shape:
+            elements *= extent
+        self._backing = torch.full((elements + 2 * GUARD_ELEMENTS,), POISON, dtype=torch.int32, device=device)
+        self.tensor = self._backing[GUARD_ELEMENTS:GUARD_ELEMENTS + elements].view(*shape)
+
+    def intact(self) -> bool:
+        guards = (self._backing[:GUARD_ELEMENTS], self._backing[-GUARD_ELEMENTS:])
+        return all(bool((g == POISON).all()) for g in guards)
 
 
-def _guards_clean(storage) -> bool:
-    return bool((storage[:GUARD_ELEMENTS] == 0).all() and (storage[-GUARD_ELEMENTS:] == 0).all())
-
-
-def _launcher(arm, req, table, tokens, out, counts, workspace, geometry, tile_size):
-    common = {
-        "block_size": geometry["block_size"],
-        "dcp_size": geometry["dcp_size"],
-        "dcp_rank": geometry["dcp_rank"],
-        "dcp_interleave": geometry["dcp_interleave"],
-    }
+def _converter(arm: str, tensors: dict, geometry: dict[str, int], tile_size: int) -> Callable[[], None]:
+    """The public launcher of ``arm`` bound to one set of device tensors."""
+    kw = {key: geometry[key] for key in _GEOMETRY_KEYS}
     if arm == "row_stable":
-        return lambda: localize_rowwise(req, table, tokens, out, counts, **common)
-    return lambda: localize_hierarchical(
-        req,
-        table,
-        tokens,
-        out,
-        counts,
-        workspace["mapped"],
-        workspace["local_positions"],
-        workspace["tile_counts"],
-        workspace["tile_offsets"],
-        tile_size=tile_size,
-        **common,
-    )
+        return lambda: localize_rowwise(tensors["req"], tensors["table"], tensors["tokens"],
+                                        tensors["out"], tensors["counts"], **kw)
+    if arm == "hierarchical_stable":
+        return lambda: localize_hierarchical(
+            tensors["req"], tensors["table"], tensors["tokens"], tensors["out"], tensors["counts"],
+            tensors["mapped"], tensors["local_positions"], tensors["tile_counts"], tensors["tile_offsets"],
+            tile_size=tile_size, **kw)
+    raise LocalizationError(f"unknown arm: {arm}")
+
+
+class _Fixture:
+    """Everything one cell's checks share: the adversarial case, its device
+    buffers (outputs and workspace inside sentinel guards, input copies kept
+    for the immutability check), the expected result and the launcher."""
+
+    def __init__(self, torch, arm, geometry, *, batch, seed, tile_size, device):
+        self.torch = torch
+        self.geometry = dict(geometry)
+        width = geometry["width"]
+        self.req_ids, self.block_table, self.rows = _random_case(
+            width=width, batch=batch, block_size=geometry["block_size"],
+            dcp_size=geometry["dcp_size"], seed=seed)
+        self.expected = localize_reference(self.req_ids, self.block_table, self.rows,
+                                           **{key: geometry[key] for key in _GEOMETRY_KEYS})
+        as_device = (lambda values: torch.tensor(values, dtype=torch.int32, device=device))
+        inputs = {"req": as_device(self.req_ids), "table": as_device(self.block_table),
+                  "tokens": as_device(self.rows)}
+        self.pristine = {name: t.clone() for name, t in inputs.items()}
+        shapes = {"out": (batch, width), "counts": (batch,)}
+        if arm == "hierarchical_stable":
+            shapes.update(workspace_shapes(batch, width, tile_size=tile_size))
+        self.guarded = {name: _Guarded(torch, shape, device) for name, shape in shapes.items()}
+        self.tensors = {**inputs, **{name: g.tensor for name, g in self.guarded.items()}}
+        self.launch = _converter(arm, self.tensors, geometry, tile_size)
+
+    def run(self):
+        """Launch once and return (out, counts) as lists."""
+        self.launch()
+        self.torch.cuda.synchronize()
+        return self.tensors["out"].cpu().tolist(), self.tensors["counts"].cpu().tolist()
+
+    def pointers(self) -> list[int]:
+        return [t.data_ptr() for t in self.tensors.values()]
+
+
+def _check_oracle(fx: _Fixture) -> bool:
+    return fx.run() == (fx.expected[0], fx.expected[1])
+
+
+def _check_order(fx: _Fixture) -> bool:
+    out, counts = fx.run()
+    g = fx.geometry
+    if g["dcp_size"] == 1:  # no compaction: every column keeps its own value
+        return out == fx.expected[0]
+    kw = {key: g[key] for key in _GEOMETRY_KEYS}
+    for row_out, count, row, req in zip(out, counts, fx.rows, fx.req_ids, strict=True):
+        want = _expected_order(row, fx.block_table[req], **kw)
+        if row_out[:count] != want or set(row_out[count:]) - {-1}:
+            return False
+    return True
+
+
+def _check_determinism(fx: _Fixture) -> bool:
+    first = fx.run()
+    return all(fx.run() == first for _ in range(DETERMINISM_REPEATS))
+
+
+def _check_replay(fx: _Fixture) -> bool:
+    torch = fx.torch
+    before = fx.pointers()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # warm up outside the default stream before capture
+        for _ in range(3):
+            fx.launch()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fx.launch()
+    allocated = torch.cuda.memory_allocated()
+    fx.tensors["out"].fill_(POISON)
+    for _ in range(REPLAY_COUNT):
+        graph.replay()
+    torch.cuda.synchronize()
+    stable = torch.cuda.memory_allocated() == allocated and fx.pointers() == before
+    result = fx.tensors["out"].cpu().tolist()
+    del graph
+    return stable and result == fx.expected[0]
+
+
+def _check_immutability(fx: _Fixture) -> bool:
+    torch = fx.torch
+    unchanged = all(bool(torch.equal(fx.tensors[name], copy)) for name, copy in fx.pristine.items())
+    return unchanged and all(g.intact() for g in fx.guarded.values())
+
+
+#: The checks of a cell, applied in this order to one fixture.
+_CHECK_FUNCTIONS: tuple[tuple[str, Callable[[_Fixture], bool]], ...] = (
+    ("oracle", _check_oracle),
+    ("order", _check_order),
+    ("determinism", _check_determinism),
+    ("replay", _check_replay),
+    ("immutability", _check_immutability),
+)
+assert tuple(name for name, _ in _CHECK_FUNCTIONS) == CHECKS
 
 
 def _run_cell(torch, arm, geometry, *, batch, seed, tile_size, device) -> CellReport:
-    report = CellReport(arm=arm, geometry=dict(geometry))
-    width = geometry["width"]
-    req_ids, block_table, rows = _random_case(
-        width=width,
-        batch=batch,
-        block_size=geometry["block_size"],
-        dcp_size=geometry["dcp_size"],
-        seed=seed,
-    )
-    req = torch.tensor(req_ids, dtype=torch.int32, device=device)
-    table = torch.tensor(block_table, dtype=torch.int32, device=device)
-    tokens = torch.tensor(rows, dtype=torch.int32, device=device)
-    tokens_before = tokens.clone()
-    table_before = table.clone()
-    out, out_storage = _guarded(torch, (batch, width), device)
-    counts, counts_storage = _guarded(torch, (batch,), device)
-    guards = [out_storage, counts_storage]
-    workspace: dict[str, object] = {}
-    if arm == "hierarchical_stable":
-        for name, shape in workspace_shapes(batch, width, tile_size=tile_size).items():
-            view, storage = _guarded(torch, shape, device)
-            workspace[name] = view
-            guards.append(storage)
-    launch = _launcher(arm, req, table, tokens, out, counts, workspace, geometry, tile_size)
-
+    report = CellReport(arm=arm, geometry=dict(geometry), checks=dict.fromkeys(CHECKS, False))
     try:
-        launch()
-        torch.cuda.synchronize()
-        observed_out = out.cpu().tolist()
-        observed_counts = counts.cpu().tolist()
-        expected_out, expected_counts = localize_reference(
-            req_ids,
-            block_table,
-            rows,
-            block_size=geometry["block_size"],
-            dcp_size=geometry["dcp_size"],
-            dcp_rank=geometry["dcp_rank"],
-            dcp_interleave=geometry["dcp_interleave"],
-        )
-        report.checks["oracle"] = observed_out == expected_out and observed_counts == expected_counts
-
-        if geometry["dcp_size"] == 1:
-            report.checks["order"] = observed_out == expected_out
-        else:
-            order_ok = True
-            for index, row in enumerate(rows):
-                want = _expected_order(
-                    row,
-                    block_table[req_ids[index]],
-                    block_size=geometry["block_size"],
-                    dcp_size=geometry["dcp_size"],
-                    dcp_rank=geometry["dcp_rank"],
-                    dcp_interleave=geometry["dcp_interleave"],
-                )
-                count = observed_counts[index]
-                if observed_out[index][:count] != want or any(
-                    v != -1 for v in observed_out[index][count:]
-                ):
-                    order_ok = False
-                    break
-            report.checks["order"] = order_ok
-
-        first = out.clone()
-        stable = True
-        for _ in range(DETERMINISM_REPEATS):
-            launch()
-            torch.cuda.synchronize()
-            if not bool(torch.equal(out, first)):
-                stable = False
-                break
-        report.checks["determinism"] = stable
-
-        pointers = [t.data_ptr() for t in (req, table, tokens, out, counts)]
-        pointers += [t.data_ptr() for t in workspace.values()]
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(3):
-                launch()
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            launch()
-        allocated_before = torch.cuda.memory_allocated()
-        for _ in range(REPLAY_COUNT):
-            graph.replay()
-        torch.cuda.synchronize()
-        after = [t.data_ptr() for t in (req, table, tokens, out, counts)]
-        after += [t.data_ptr() for t in workspace.values()]
-        report.checks["replay"] = (
-            torch.cuda.memory_allocated() == allocated_before
-            and after == pointers
-            and out.cpu().tolist() == expected_out
-        )
-        del graph
-
-        report.checks["immutability"] = (
-            bool(torch.equal(tokens, tokens_before))
-            and bool(torch.equal(table, table_before))
-            and all(_guards_clean(storage) for storage in guards)
-        )
+        fixture = _Fixture(torch, arm, geometry, batch=batch, seed=seed, tile_size=tile_size, device=device)
+        for name, check in _CHECK_FUNCTIONS:
+            report.checks[name] = bool(check(fixture))
     except Exception as exc:  # reported, not raised
         report.error = f"{type(exc).__name__}: {exc}"
-
-    for name in CHECKS:
-        report.checks.setdefault(name, False)
     return report
 
 
@@ -361,35 +376,38 @@ def conformance(
 
     ``matrix`` holds geometry dicts with ``width``, ``block_size``,
     ``dcp_size``, ``dcp_rank`` and ``dcp_interleave`` (default
-    :data:`DEFAULT_MATRIX`); every cell derives its own seed from ``seed``.
-    Without torch or a CUDA device the report is skipped (falsy, with a
-    reason) rather than raising, so it is safe to call in CI.
+    :data:`DEFAULT_MATRIX`); the cell of geometry ``i`` uses seed ``seed + i``
+    in every arm. Without torch or a CUDA device the report is skipped (falsy,
+    with a reason) rather than raising, so it is safe to call in CI.
     """
-    report = ConformanceReport()
+    unknown = [arm for arm in arms if arm not in ARMS]
+    if unknown:
+        raise LocalizationError(f"unknown arm: {unknown[0]}")
     try:
         import torch
     except ModuleNotFoundError:
         torch = None
     reason = _skip_reason(torch)
     if reason is not None:
-        report.skipped = reason
-        return report
-    report.device = torch.cuda.get_device_name(0)
-    cells = tuple(DEFAULT_MATRIX if matrix is None else matrix)
-    for arm in arms:
-        if arm not in ARMS:
-            raise LocalizationError(f"unknown arm: {arm}")
-        for index, geometry in enumerate(cells):
-            report.cells.append(
-                _run_cell(torch, arm, geometry, batch=batch, seed=seed + index, tile_size=tile_size,
-                          device="cuda")
-            )
-    return report
+        return ConformanceReport(skipped=reason)
+    cells = DEFAULT_MATRIX if matrix is None else tuple(matrix)
+    return ConformanceReport(
+        device=torch.cuda.get_device_name(0),
+        cells=[_run_cell(torch, arm, geometry, batch=batch, seed=seed + index, tile_size=tile_size,
+                         device="cuda")
+               for arm in arms for index, geometry in enumerate(cells)],
+    )
 
 
 @dataclass
 class ReplayGateReport:
-    """Outcome of :func:`replay_gate`."""
+    """Outcome of :func:`replay_gate` or :func:`decode_step_gate`.
+
+    ``mismatches`` sums the device counters over every replay (and, for a
+    step, every layer); ``layer_mismatches`` holds the per-layer counters of a
+    step. Each checkpoint records ``pointers``, ``allocated``, ``reserved``
+    and ``exact`` (no mismatch so far) at that replay count.
+    """
 
     arm: str
     geometry: dict[str, int]
@@ -397,6 +415,9 @@ class ReplayGateReport:
     mismatches: int = -1
     checkpoints: dict[int, dict[str, bool]] = field(default_factory=dict)
     error: str | None = None
+    layers: int = 1
+    layer_mismatches: list[int] = field(default_factory=list)
+    step_us: float | None = None
 
     @property
     def ok(self) -> bool:
@@ -406,6 +427,44 @@ class ReplayGateReport:
             and bool(self.checkpoints)
             and all(all(c.values()) for c in self.checkpoints.values())
         )
+
+
+def _replay_with_checkpoints(torch, graph, replays, checkpoints, buffers, counters, report) -> None:
+    """Replay ``graph`` ``replays`` times, recording the pointer, allocator and
+    counter state at each checkpoint (0 = right after capture)."""
+    pointers = [t.data_ptr() for t in buffers]
+    allocated = torch.cuda.memory_allocated()
+    reserved = torch.cuda.memory_reserved()
+    done = 0
+    for mark in sorted({c for c in checkpoints if 0 <= c <= replays}) + [replays]:
+        while done < mark:
+            graph.replay()
+            done += 1
+        torch.cuda.synchronize()
+        if mark in checkpoints:
+            report.checkpoints[mark] = {
+                "pointers": [t.data_ptr() for t in buffers] == pointers,
+                "allocated": torch.cuda.memory_allocated() == allocated,
+                "reserved": torch.cuda.memory_reserved() == reserved,
+                "exact": int(counters.sum().item()) == 0,
+            }
+    report.replays = done
+
+
+def _capture(torch, step) -> object:
+    """Warm ``step`` up on a side stream, then capture it into a CUDA graph."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    torch.cuda.synchronize()
+    return graph
 
 
 def replay_gate(
@@ -423,95 +482,128 @@ def replay_gate(
     The graph holds: ``out`` and ``counts`` overwritten with a poison value,
     the localization call, and two device-side compares against the oracle's
     result that add into a preallocated mismatch counter. Pointers and
-    ``torch.cuda.memory_allocated()`` are compared with their values before
-    the first replay at every checkpoint (0 = right after capture).
+    ``torch.cuda.memory_allocated()`` / ``memory_reserved()`` are compared
+    with their values after capture at every checkpoint (0 = right after
+    capture).
     """
     import torch
 
-    report = ReplayGateReport(arm=arm, geometry=dict(geometry))
     if arm not in ARMS:
         raise LocalizationError(f"unknown arm: {arm}")
-    width = geometry["width"]
-    req_ids, block_table, rows = _random_case(
-        width=width,
-        batch=batch,
-        block_size=geometry["block_size"],
-        dcp_size=geometry["dcp_size"],
-        seed=seed,
-    )
-    expected_out, expected_counts = localize_reference(
-        req_ids,
-        block_table,
-        rows,
-        block_size=geometry["block_size"],
-        dcp_size=geometry["dcp_size"],
-        dcp_rank=geometry["dcp_rank"],
-        dcp_interleave=geometry["dcp_interleave"],
-    )
-    device = "cuda"
-    req = torch.tensor(req_ids, dtype=torch.int32, device=device)
-    table = torch.tensor(block_table, dtype=torch.int32, device=device)
-    tokens = torch.tensor(rows, dtype=torch.int32, device=device)
-    want_out = torch.tensor(expected_out, dtype=torch.int32, device=device)
-    want_counts = torch.tensor(expected_counts, dtype=torch.int32, device=device)
-    out = torch.empty_like(tokens)
-    counts = torch.empty(batch, dtype=torch.int32, device=device)
-    mismatches = torch.zeros(1, dtype=torch.int32, device=device)
-    workspace: dict[str, object] = {}
-    if arm == "hierarchical_stable":
-        workspace = {
-            name: torch.empty(shape, dtype=torch.int32, device=device)
-            for name, shape in workspace_shapes(batch, width, tile_size=tile_size).items()
-        }
-    launch = _launcher(arm, req, table, tokens, out, counts, workspace, geometry, tile_size)
-
-    def step() -> None:
-        out.fill_(POISON)
-        counts.fill_(POISON)
-        launch()
-        count_mismatches(out, want_out, mismatches)
-        count_mismatches(counts, want_counts, mismatches)
-
+    report = ReplayGateReport(arm=arm, geometry=dict(geometry))
     try:
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(3):
-                step()
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        torch.cuda.synchronize()
-        mismatches.zero_()
-        buffers = (req, table, tokens, out, counts, mismatches, *workspace.values())
-        pointers = [t.data_ptr() for t in buffers]
-        allocated = torch.cuda.memory_allocated()
-        reserved = torch.cuda.memory_reserved()
-        marks = sorted({c for c in checkpoints if 0 <= c <= replays})
-        done = 0
-        for mark in marks:
-            while done < mark:
-                graph.replay()
-                done += 1
-            torch.cuda.synchronize()
-            report.checkpoints[mark] = {
-                "pointers": [t.data_ptr() for t in buffers] == pointers,
-                "allocated": torch.cuda.memory_allocated() == allocated,
-                "reserved": torch.cuda.memory_reserved() == reserved,
-                "exact": int(mismatches.item()) == 0,
-            }
-        while done < replays:
-            graph.replay()
-            done += 1
-        torch.cuda.synchronize()
-        report.replays = done
-        report.mismatches = int(mismatches.item())
+        fixture = _Fixture(torch, arm, geometry, batch=batch, seed=seed, tile_size=tile_size, device="cuda")
+        want_out = torch.tensor(fixture.expected[0], dtype=torch.int32, device="cuda")
+        want_counts = torch.tensor(fixture.expected[1], dtype=torch.int32, device="cuda")
+        counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+        out, counts = fixture.tensors["out"], fixture.tensors["counts"]
+
+        def step() -> None:
+            out.fill_(POISON)
+            counts.fill_(POISON)
+            fixture.launch()
+            count_mismatches(out, want_out, counter)
+            count_mismatches(counts, want_counts, counter)
+
+        graph = _capture(torch, step)
+        counter.zero_()
+        buffers = [*fixture.tensors.values(), counter]
+        _replay_with_checkpoints(torch, graph, replays, set(checkpoints), buffers, counter, report)
+        report.mismatches = int(counter.item())
         del graph
     except Exception as exc:  # reported, not raised
         report.error = f"{type(exc).__name__}: {exc}"
     return report
+
+
+def decode_step_gate(
+    layers: Sequence,
+    *,
+    expected: Sequence | None = None,
+    replays: int = GATE_REPLAYS,
+    checkpoints: Sequence[int] = GATE_CHECKPOINTS,
+    timing_replays: int = 100,
+) -> ReplayGateReport:
+    """Replay a whole captured decode step ``replays`` times and check every
+    layer of every replay.
+
+    ``layers`` holds one ``silkern_b200.workloads.Case`` per layer (its own
+    inputs; all layers of one shape and geometry, row-wise); ``expected``
+    optionally holds each layer's (out, counts), else they come from
+    :func:`localize_reference` (pure Python, a few seconds for a full step).
+    The step graph
+    poisons every layer's output, runs one converter call per layer, and
+    compares all outputs and counts with the oracle's on the device in two
+    launches that add into one counter per layer. Per-step converter time is
+    measured separately, from a graph of the converter calls alone replayed
+    ``timing_replays`` times between CUDA events.
+    """
+    import numpy as np
+    import torch
+
+    first = layers[0]
+    geometry = {"width": first.width, **first.geometry()}
+    report = ReplayGateReport(arm="row_stable", geometry=geometry, layers=len(layers))
+    try:
+        n, batch, width = len(layers), first.batch, first.width
+        dev = "cuda"
+        outs = torch.full((n, batch, width), POISON, dtype=torch.int32, device=dev)
+        counts = torch.full((n, batch), POISON, dtype=torch.int32, device=dev)
+        want_out = np.empty((n, batch, width), dtype=np.int32)
+        want_counts = np.empty((n, batch), dtype=np.int32)
+        inputs = []
+        for index, case in enumerate(layers):
+            if case.tokens.shape != (batch, width) or case.geometry() != first.geometry():
+                raise LocalizationError("every layer of a step needs one shape and geometry")
+            want_out[index], want_counts[index] = (expected[index] if expected is not None
+                                                   else _contract_result(case))
+            inputs.append(tuple(torch.as_tensor(a).to(dev) for a in (case.req_ids, case.block_table, case.tokens)))
+        want_out_d = torch.as_tensor(want_out).to(dev)
+        want_counts_d = torch.as_tensor(want_counts).to(dev)
+        counters = torch.zeros(n, dtype=torch.int32, device=dev)
+        kw = first.geometry()
+
+        def convert() -> None:
+            for index, (req, table, tokens) in enumerate(inputs):
+                localize_rowwise(req, table, tokens, outs[index], counts[index], **kw)
+
+        def step() -> None:
+            outs.fill_(POISON)
+            counts.fill_(POISON)
+            convert()
+            count_segment_mismatches(outs, want_out_d, counters)
+            count_segment_mismatches(counts, want_counts_d, counters)
+
+        graph = _capture(torch, step)
+        counters.zero_()
+        buffers = [outs, counts, counters, want_out_d, want_counts_d, *(t for layer in inputs for t in layer)]
+        _replay_with_checkpoints(torch, graph, replays, set(checkpoints), buffers, counters, report)
+        report.layer_mismatches = [int(v) for v in counters.cpu().tolist()]
+        report.mismatches = sum(report.layer_mismatches)
+        del graph
+
+        timing = _capture(torch, convert)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(timing_replays):
+            timing.replay()
+        end.record()
+        torch.cuda.synchronize()
+        report.step_us = start.elapsed_time(end) * 1e3 / timing_replays
+        del timing
+    except Exception as exc:  # reported, not raised
+        report.error = f"{type(exc).__name__}: {exc}"
+    return report
+
+
+def _contract_result(case):
+    """(out, counts) of one workload case from :func:`localize_reference`."""
+    import numpy as np
+
+    out, counts = localize_reference(case.req_ids.tolist(), case.block_table.tolist(), case.tokens.tolist(),
+                                     **case.geometry())
+    return np.asarray(out, dtype=np.int32), np.asarray(counts, dtype=np.int32)
 
 
 def main(argv: Sequence[str] | None = None) -> int:  # pragma: no cover - CLI

@@ -1,6 +1,6 @@
 """Generate the golden fixtures from the reference implementation itself.
 
-    python tests/golden/make_golden.py [--reference /root/reference] [--skip-config5]
+    python tests/golden/make_golden.py --reference <checkout of the reference> [--skip-config5]
 
 Runs in a container that has the reference checkout (read-only is fine) and
 triton; it is not needed on a GPU machine. For every case it records the
@@ -150,7 +150,8 @@ def record(np, torch, entry, req_ids, block_table, rows, *, geometry, compact=Tr
 
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True,
+                        help="path of a checkout of the reference repository (its silkern package)")
     parser.add_argument("--skip-config5", action="store_true")
     args = parser.parse_args(argv)
     _setup(args.reference)

@@ -141,6 +141,36 @@ def test_hierarchical_rejects_before_launch(lib) -> None:
     assert call(128, to=0xD0000) == 6
 
 
+def test_noalloc_checks_arguments_in_the_workspace_entry_points_order(lib) -> None:
+    """The allocation-free entry point rejects bad arguments with the same
+    codes, in the same order, as the workspace entry point, and only then
+    applies its own static-array limit (batch x tiles)."""
+    far = 1 << 40  # fake buffers this far apart never overlap, whatever the shapes
+
+    def call(req=REQ, out=3 * far, batch=4, width=16, dcp=2, tile=128):
+        return lib.silkern_localize_hierarchical_noalloc_v1(
+            req, far, 4, 8, 2 * far, out, 4 * far, batch, width, 64, dcp, 0, 1, 1, tile, None, None,
+        )
+
+    huge = 1 << 20  # batch x tiles far beyond the static array
+    assert call(req=None, batch=huge) == 1
+    assert call(out=None, batch=huge) == 1
+    assert call(dcp=0, batch=huge) == 3
+    assert call(tile=96, batch=huge) == 5
+    assert call(out=2 * far, batch=4) == 6
+    assert call(batch=huge, width=16384) == 8
+    assert call(batch=40000, width=64, tile=64) == 8
+
+
+def test_segment_mismatch_counter_rejects(lib) -> None:
+    call = lib.silkern_count_segment_mismatches_v1
+    assert call(None, TOK, 4, 16, CNT, None) == 1
+    assert call(OUT, TOK, 4, 16, None, None) == 1
+    assert call(OUT, TOK, 65536, 16, CNT, None) == 2
+    assert call(OUT, TOK, -1, 16, CNT, None) == 2
+    assert call(OUT, TOK, 0, 16, CNT, None) == 0  # nothing to compare: no launch
+
+
 def test_explicit_rejects_bad_geometry(lib) -> None:
     def call(cluster, stage=-1, prefetch=-1, width=16, chunks=0):
         return lib.silkern_localize_explicit_v1(
