@@ -22,6 +22,7 @@ a machine without it.
 from __future__ import annotations
 
 import contextlib
+import sys
 from numbers import Integral
 
 from silkern_b200 import _native
@@ -89,10 +90,36 @@ def _check_status(torch, status, device):
     return status.data_ptr()
 
 
+def _ensure_ops() -> None:
+    """Register the torch.library ops on the first eager launch, so a later
+    torch.compile of the caller finds them."""
+    from silkern_b200 import ops
+
+    if not ops.registered():
+        ops.register()
+
+
 def _device_scope(torch, device):
     if device.index is None or device.index == torch.cuda.current_device():
         return contextlib.nullcontext()
     return torch.cuda.device(device)
+
+
+def _compiling(torch) -> bool:
+    """True while torch.compile traces the caller."""
+    compiler = getattr(torch, "compiler", None)
+    return bool(compiler is not None and compiler.is_compiling())
+
+
+def _traced_op(torch, name: str):
+    from silkern_b200 import ops
+
+    if not ops.registered():
+        raise LocalizationError(
+            "silkern_b200 ops are not registered: call silkern_b200.ops.register() (or launch once "
+            "eagerly) before compiling"
+        )
+    return getattr(torch.ops.silkern_b200, name)
 
 
 def localize_rowwise(
@@ -120,8 +147,43 @@ def localize_rowwise(
     ``SILKERN_STATUS_BAD_REQUEST`` if a request id is outside the block table;
     such a row is emitted as all ``-1`` with count 0.
 
+    Under ``torch.compile`` the call is the custom op
+    ``torch.ops.silkern_b200.localize_rowwise`` (one opaque node, checked and
+    launched when the compiled code runs); otherwise the C ABI is called
+    directly.
+
     Raises :class:`LocalizationError` on any unsupported geometry or binding.
     """
+    import torch
+
+    if _compiling(torch):
+        _traced_op(torch, "localize_rowwise")(
+            req_ids, block_table, tokens, out, counts, block_size, dcp_size, dcp_rank, dcp_interleave,
+            compact_valid_to_front, num_warps, status)
+        return
+    _ensure_ops()
+    _rowwise_eager(req_ids, block_table, tokens, out, counts, block_size=block_size, dcp_size=dcp_size,
+                   dcp_rank=dcp_rank, dcp_interleave=dcp_interleave,
+                   compact_valid_to_front=compact_valid_to_front, num_warps=num_warps, status=status)
+
+
+def _rowwise_eager(
+    req_ids,
+    block_table,
+    tokens,
+    out,
+    counts,
+    *,
+    block_size: int,
+    dcp_size: int,
+    dcp_rank: int,
+    dcp_interleave: int = 1,
+    compact_valid_to_front: bool = True,
+    num_warps: int = 8,
+    status=None,
+) -> None:
+    """The reference's checks for localize_rowwise (kernels.py:351-409), then
+    one C ABI call on the current stream."""
     import torch
 
     tensors = (req_ids, block_table, tokens, out, counts)
@@ -197,7 +259,49 @@ def localize_hierarchical(
     elements in tile ``k`` of row ``r`` and ``tile_offsets_workspace[r, k]``
     their exclusive prefix; ``mapped_workspace`` and
     ``local_positions_workspace`` are validated but not touched.
+
+    Under ``torch.compile`` the call is the custom op
+    ``torch.ops.silkern_b200.localize_hierarchical``; otherwise the C ABI is
+    called directly.
     """
+    import torch
+
+    if _compiling(torch):
+        _traced_op(torch, "localize_hierarchical")(
+            req_ids, block_table, tokens, out, counts, mapped_workspace, local_positions_workspace,
+            tile_counts_workspace, tile_offsets_workspace, block_size, dcp_size, dcp_rank, dcp_interleave,
+            compact_valid_to_front, tile_size, num_warps, status)
+        return
+    _ensure_ops()
+    _hierarchical_eager(req_ids, block_table, tokens, out, counts, mapped_workspace,
+                        local_positions_workspace, tile_counts_workspace, tile_offsets_workspace,
+                        block_size=block_size, dcp_size=dcp_size, dcp_rank=dcp_rank,
+                        dcp_interleave=dcp_interleave, compact_valid_to_front=compact_valid_to_front,
+                        tile_size=tile_size, num_warps=num_warps, status=status)
+
+
+def _hierarchical_eager(
+    req_ids,
+    block_table,
+    tokens,
+    out,
+    counts,
+    mapped_workspace,
+    local_positions_workspace,
+    tile_counts_workspace,
+    tile_offsets_workspace,
+    *,
+    block_size: int,
+    dcp_size: int,
+    dcp_rank: int,
+    dcp_interleave: int = 1,
+    compact_valid_to_front: bool = True,
+    tile_size: int = DEFAULT_TILE_SIZE,
+    num_warps: int = 4,
+    status=None,
+) -> None:
+    """The reference's checks for localize_hierarchical (kernels.py:467-558),
+    then one C ABI call on the current stream."""
     import torch
 
     tensors = (
@@ -366,4 +470,10 @@ def count_segment_mismatches(a, b, counters) -> None:
             a.data_ptr(), b.data_ptr(), segments, a.numel() // max(segments, 1), counters.data_ptr(), stream
         )
     _native.check(code, "count_segment_mismatches")
+
+
+if "torch" in sys.modules:  # torch is already loaded: define the ops now (see silkern_b200.ops)
+    from silkern_b200 import ops as _ops
+
+    _ops.register()
 

@@ -616,3 +616,47 @@ def test_cluster_noncompacting_and_bad_requests(cluster, tile_size) -> None:
     assert np.array_equal(out[good], want[0]) and np.array_equal(counts[good], want[1])
     assert np.all(out[[1, 4]] == -1) and np.all(counts[[1, 4]] == 0)
     assert int(status.item()) == 1
+
+
+def test_compiled_launchers_inside_a_cuda_graph_are_bit_exact() -> None:
+    """torch.compile(fullgraph=True) around both public launchers (traced as
+    the silkern_b200 custom ops, no graph break), the compiled function then
+    captured in a CUDA graph and replayed: outputs bit-exact with the oracle
+    after every replay."""
+    from silkern_b200 import ops
+
+    ops.register()
+    case = config_case(3, seed=77, dcp_rank=2, batch=32)
+    kw = case.geometry()
+    req, table, tokens = (_cuda(a) for a in (case.req_ids, case.block_table, case.tokens))
+    want_out, want_counts = _oracle(case.req_ids, case.block_table, case.tokens, **kw)
+    out, counts = torch.empty_like(tokens), torch.empty(case.batch, dtype=torch.int32, device=DEV)
+    out2, counts2 = torch.empty_like(tokens), torch.empty_like(counts)
+    ws = [torch.empty(s, dtype=torch.int32, device=DEV)
+          for s in workspace_shapes(case.batch, case.width, tile_size=1024).values()]
+
+    def step():
+        localize_rowwise(req, table, tokens, out, counts, **kw)
+        localize_hierarchical(req, table, tokens, out2, counts2, *ws, tile_size=1024, **kw)
+
+    torch._dynamo.reset()
+    compiled = torch.compile(step, fullgraph=True)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            compiled()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        compiled()
+    for _ in range(5):
+        for t in (out, counts, out2, counts2):
+            t.fill_(0x5A5A5A5A)
+        graph.replay()
+        torch.cuda.synchronize()
+        for got_out, got_counts in ((out, counts), (out2, counts2)):
+            assert np.array_equal(got_out.cpu().numpy(), want_out)
+            assert np.array_equal(got_counts.cpu().numpy(), want_counts)
+    del graph
