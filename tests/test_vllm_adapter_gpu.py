@@ -73,3 +73,64 @@ def test_adapter_rejects_a_different_fixed_address_binding() -> None:
     with pytest.raises(AdapterError, match="differs from registered"):
         adapter(req_ids, block_table, tokens, 2, 1, BLOCK_SIZE=64, NUM_TOPK_TOKENS=2048,
                 return_valid_counts=True)
+
+
+def test_installed_adapter_inside_a_captured_stand_in_decode_step() -> None:
+    """The adapter installed at a stand-in module's converter attribute and
+    called from a stand-in sparse-attention step (converter, then a gather of
+    a fake KV cache at the returned slots, masked by the counts). The whole
+    step is captured once; every replay gets a fresh selection written into
+    the bound token buffer, as the upstream top-k would, and its result is
+    checked against the contract on the host."""
+    from types import SimpleNamespace
+
+    import numpy as np
+
+    from silkern_b200.integrations.vllm import install_converter
+
+    def upstream(*args, **kwargs):
+        raise AssertionError("the upstream converter must not run while the adapter is installed")
+
+    module = SimpleNamespace(triton_filter_and_convert_dcp_index=upstream)
+    req_list, table_list, _ = _case()
+    req_ids = torch.tensor(req_list, dtype=torch.int32, device="cuda")
+    block_table = torch.tensor(table_list, dtype=torch.int32, device="cuda")
+    tokens = torch.zeros((3, 2048), dtype=torch.int32, device="cuda")
+    kv = torch.arange(8192, dtype=torch.int64, device="cuda") * 3 + 1
+    result = torch.zeros(3, dtype=torch.int64, device="cuda")
+    columns = torch.arange(2048, device="cuda")
+    adapter = WorkspaceAdapter("row_stable")
+    adapter.prepare(req_ids, block_table, tokens, dcp_size=2, dcp_rank=1, block_size=64)
+
+    def sparse_attention_step() -> None:
+        out, counts = module.triton_filter_and_convert_dcp_index(
+            req_ids, block_table, tokens, 2, 1, 1, BLOCK_SIZE=64, NUM_TOPK_TOKENS=2048, BLOCK_N=128,
+            return_valid_counts=True)
+        valid = columns[None, :] < counts[:, None]
+        result.copy_((kv[out.clamp_min(0).long()] * valid).sum(dim=1))
+
+    rng = np.random.default_rng(31)
+    with install_converter(module, adapter):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                sparse_attention_step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            sparse_attention_step()
+        for _ in range(30):
+            selection = rng.integers(-2, 4096, size=(3, 2048), dtype=np.int32)
+            tokens.copy_(torch.as_tensor(selection))
+            graph.replay()
+            torch.cuda.synchronize()
+            want_out, want_counts = exact_stable_compact_reference(
+                req_list, table_list, selection.tolist(), block_size=64, dcp_size=2, dcp_rank=1,
+                dcp_interleave=1)
+            assert adapter.output.cpu().tolist() == want_out
+            want = [sum(int(kv[s]) for s in row[:n]) for row, n in zip(want_out, want_counts, strict=True)]
+            assert result.cpu().tolist() == want
+        del graph
+    assert module.triton_filter_and_convert_dcp_index is upstream
