@@ -661,15 +661,14 @@ void smem_limits(int* per_sm, int* reserved) {
   *reserved = cache_res[dev];
 }
 
-// Columns per thread and threads for `slice` columns: the shortest run that
-// covers the slice with at most kMaxThreads threads, starting from 8 columns
-// on one CTA and 16 across a cluster (measured the faster starts), unless
-// run_req pins it (4, 8, 16 or 32). Threads are a whole number of warps; a
-// row group (no cluster) is a power of two of them.
+// Columns per thread and threads for `slice` columns: the shortest run from
+// 8 columns up that covers the slice with at most kMaxThreads threads,
+// unless run_req pins it (4, 8, 16 or 32). Threads are a whole number of
+// warps; a row group (no cluster) is a power of two of them.
 bool fit_slice(int slice, int run_req, bool cluster, int* run, int* threads) {
   int g = run_req;
   if (g == 0) {
-    g = cluster ? 16 : 8;
+    g = 8;
     while (g < 32 && (slice + g - 1) / g > kMaxThreads) g *= 2;
   }
   int t = (slice + g - 1) / g;
@@ -887,6 +886,16 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req, i
   p.smem_tile = g.smem_tile;
   p.smem_group = g.smem_group;
   size_t smem = sizeof(int32_t) * static_cast<size_t>(p.smem_group) * static_cast<size_t>(g.rows_per_cta);
+  if (g.cluster > 1) {
+    // One cluster CTA per SM. With two, the next call's clusters (launched
+    // early by programmatic dependent launch) share the SMs of the running
+    // call; one per SM measured 4.05 -> 3.45 us per call at 32 rows x 16384
+    // columns over four-CTA clusters.
+    int per_sm = 0, reserved = 0;
+    smem_limits(&per_sm, &reserved);
+    const size_t one_per_sm = static_cast<size_t>(per_sm / 2 - reserved + 16);
+    if (smem < one_per_sm) smem = one_per_sm;
+  }
   if (g.cluster == 1 && grid <= sm_count()) {
     // At most two CTAs of this kernel per SM: the running call and the next
     // one waiting on it, so the next call's CTAs spread over the SMs instead
