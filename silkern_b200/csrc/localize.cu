@@ -191,7 +191,7 @@ __host__ __device__ constexpr int count_bits(int g) { return g < 2 ? 1 : 1 + cou
 // become resident where this call left room, and with one-row CTAs several of
 // them could pile onto one SM.
 template <int G, bool CLUSTER, int MODE, bool COMPACT, bool STAGE>
-__global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 8) ? 1 : 2)
+__global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
     localize_kernel(const __grid_constant__ Params p) {
   // per row group: [staged table row][staged output][warp totals][tile offsets]
   extern __shared__ __align__(16) int32_t smem[];
@@ -359,14 +359,16 @@ __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 8) ? 1 : 2)
       lb = local >> p.bs_shift;
       off = local & p.bs_mask;
     }
-    const bool ok = (bits >> j) & 1u;
-    int32_t b = 0;
+    int32_t b;
     if constexpr (STAGE) {
-      if (ok) b = s_tbl[lb];
+      b = 0;
+      if ((bits >> j) & 1u) b = s_tbl[lb];
     } else {
       b = blk[j];
     }
-    v[j] = ok ? static_cast<int32_t>(static_cast<uint32_t>(b) * p.block_size + off) : -1;
+    const int32_t phys = static_cast<int32_t>(static_cast<uint32_t>(b) * p.block_size + off);
+    // A compacting call never stores an invalid element: no select needed.
+    v[j] = (COMPACT || ((bits >> j) & 1u)) ? phys : -1;
   }
 
   // Hierarchical: the CTA-local exclusive position of each tile's first
@@ -662,13 +664,14 @@ void smem_limits(int* per_sm, int* reserved) {
 }
 
 // Columns per thread and threads for `slice` columns: the shortest run from
-// 8 columns up that covers the slice with at most kMaxThreads threads,
-// unless run_req pins it (4, 8, 16 or 32). Threads are a whole number of
-// warps; a row group (no cluster) is a power of two of them.
-bool fit_slice(int slice, int run_req, bool cluster, int* run, int* threads) {
+// `first` columns up (8, or 16 for batches of several waves) that covers the
+// slice with at most kMaxThreads threads, unless run_req pins it (4, 8, 16
+// or 32). Threads are a whole number of warps; a row group (no cluster) is a
+// power of two of them.
+bool fit_slice(int slice, int run_req, int first, bool cluster, int* run, int* threads) {
   int g = run_req;
   if (g == 0) {
-    g = 8;
+    g = first;
     while (g < 32 && (slice + g - 1) / g > kMaxThreads) g *= 2;
   }
   int t = (slice + g - 1) / g;
@@ -735,7 +738,13 @@ int choose_geometry(const Request& r, bool compact, int cluster_req, int stage_r
   }
   if (cluster_req > 0 && cs != cluster_req) return SILKERN_E_GEOMETRY;
   if (cs < 1 || cs > kMaxCluster) return SILKERN_E_GEOMETRY;
-  if (!fit_slice(slice, run_req, cs > 1, &g->run, &g->threads)) return SILKERN_E_GEOMETRY;
+  // Short runs (more warps, shorter per-thread chains) measured faster while
+  // one call's rows fit the GPU in a wave or two; once a batch takes several
+  // waves the work is issue-bound and 16-column runs, which amortise each
+  // thread's fixed instructions over twice the columns, measured faster
+  // (16384 rows x 2048: 70.7 -> 66.8 us per call).
+  const int first_run = (cs == 1 && r.batch >= int64_t{4} * sm_count()) ? 16 : 8;
+  if (!fit_slice(slice, run_req, first_run, cs > 1, &g->run, &g->threads)) return SILKERN_E_GEOMETRY;
   g->cluster = cs;
   g->slice = slice;
   g->rows_per_cta = 1;
@@ -897,13 +906,19 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req, i
     if (smem < one_per_sm) smem = one_per_sm;
   }
   if (g.cluster == 1 && grid <= sm_count()) {
-    // At most two CTAs of this kernel per SM: the running call and the next
-    // one waiting on it, so the next call's CTAs spread over the SMs instead
-    // of piling onto the ones this call left room on.
+    // Residency under programmatic dependent launch. When one call fills
+    // every SM, two CTAs per SM (the running call and the next one waiting
+    // on it) let the next call's CTAs start early and spread over the SMs
+    // instead of piling onto the ones this call left room on. When the batch
+    // leaves SMs free, one CTA per SM measured faster: the next call lands
+    // on SMs of its own (64 x 2048: 2.19 -> 1.80 us per call; 128 x 2048:
+    // 2.29 -> 1.87), while at 256 rows on 148 SMs it was slower (2.24 ->
+    // 2.34).
     int per_sm = 0, reserved = 0;
     smem_limits(&per_sm, &reserved);
-    const size_t two_per_sm = static_cast<size_t>(per_sm / 3 - reserved + 16);
-    if (smem < two_per_sm) smem = two_per_sm;
+    const int per_sm_ctas = grid < sm_count() ? 1 : 2;
+    const size_t reserve = static_cast<size_t>(per_sm / (per_sm_ctas + 1) - reserved + 16);
+    if (smem < reserve) smem = reserve;
   }
   if (smem > 48 * 1024) {
     rc = allow_large_smem(fn, smem);
