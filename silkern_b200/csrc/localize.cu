@@ -52,7 +52,6 @@ namespace silkern {
 constexpr int kMaxThreads = 512;      // threads per CTA (row groups, or one cluster slice)
 constexpr int kMaxCluster = 8;
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
-constexpr int kStageSmemMax = 96 * 1024;  // shared memory per CTA for an automatic stage
 constexpr int kSmemMax = 200 * 1024;      // dynamic shared memory per CTA, any launch
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr int kModeGeneral = 0;  // invariant-divisor multiplies
@@ -762,20 +761,14 @@ int choose_geometry(const Request& r, bool compact, int cluster_req, int stage_r
     g->rows_per_cta = static_cast<int>(rows);
     g->row_ctas = ctas;
   }
-  // Table stage: on request (rows up to kTableStageMax entries), or by
-  // default across a cluster when the row fits and the CTA's shared memory
-  // stays modest. On one CTA the L2 gather measured faster (its latency
-  // hides behind the other warps' issue, while the stage adds instructions);
-  // across a cluster the stage did (the cluster exchange leaves time to
-  // fill it).
+  // Table stage only on request (rows up to kTableStageMax entries): the L2
+  // gather measured faster by default, on one CTA (config 3: 2.24 against
+  // 2.39 us per call; its latency hides behind the other warps' issue while
+  // the stage adds instructions) and across a cluster at one CTA per SM
+  // (config 4: 3.38 against 3.45).
   if (stage_req == 1 && r.table_width > kTableStageMax) return SILKERN_E_GEOMETRY;
-  g->stage = stage_req == 1 || (stage_req < 0 && cs > 1 && r.table_width <= kTableStageMax);
+  g->stage = stage_req == 1;
   layout_smem(r, compact, g);
-  if (stage_req < 0 && g->stage &&
-      static_cast<int64_t>(g->smem_group) * 4 * g->rows_per_cta > kStageSmemMax) {
-    g->stage = false;
-    layout_smem(r, compact, g);
-  }
   if (static_cast<int64_t>(g->smem_group) * 4 * g->rows_per_cta > kSmemMax) return SILKERN_E_GEOMETRY;
   const int64_t table_bytes = r.table_rows * r.table_width * 4;
   const bool aligned = (reinterpret_cast<uintptr_t>(r.table) & 15u) == 0;
