@@ -738,20 +738,25 @@ int choose_geometry(const Request& r, bool compact, int cluster_req, int stage_r
   if (cluster_req > 0 && cs != cluster_req) return SILKERN_E_GEOMETRY;
   if (cs < 1 || cs > kMaxCluster) return SILKERN_E_GEOMETRY;
   // Short runs (more warps, shorter per-thread chains) measured faster while
-  // one call's rows fit the GPU in a wave or two; once a batch takes several
-  // waves the work is issue-bound and 16-column runs, which amortise each
+  // one call's rows fit the GPU in a few waves (600 rows of 2048: 4.64
+  // against 5.33 us per call with 16-column runs); from about six rows per
+  // SM the work is issue-bound and 16-column runs, which amortise each
   // thread's fixed instructions over twice the columns, measured faster
-  // (16384 rows x 2048: 70.7 -> 66.8 us per call).
-  const int first_run = (cs == 1 && r.batch >= int64_t{4} * sm_count()) ? 16 : 8;
+  // (1024 rows: 5.50 against 6.04; 16384 rows: 66.7 against 69.9).
+  const int first_run = (cs == 1 && r.batch >= int64_t{6} * sm_count()) ? 16 : 8;
   if (!fit_slice(slice, run_req, first_run, cs > 1, &g->run, &g->threads)) return SILKERN_E_GEOMETRY;
   g->cluster = cs;
   g->slice = slice;
   g->rows_per_cta = 1;
   g->row_ctas = r.batch;
   if (cs == 1) {
-    // Row groups: rows are packed into CTAs of up to kMaxThreads threads and
+    // Row groups. Up to four rows per SM on average, one row per CTA (the
+    // shared-memory reservation below keeps as many CTAs per SM as the batch
+    // needs, no more): 256 rows of 2048 measured 2.16 us per call against
+    // 2.24-2.41 with two-row CTAs on 148 SMs, 400 rows 2.74 against 3.12.
+    // Beyond that, rows are packed into CTAs of up to kMaxThreads threads and
     // spread over at most one CTA per SM.
-    const int64_t max_rows = kMaxThreads / g->threads;
+    const int64_t max_rows = r.batch <= int64_t{4} * sm_count() ? 1 : kMaxThreads / g->threads;
     int64_t ctas = r.batch < sm_count() ? r.batch : sm_count();
     int64_t rows = (r.batch + ctas - 1) / ctas;
     if (rows > max_rows) {
@@ -898,18 +903,18 @@ int launch(const Request& r, int cluster_req, int stage_req, int prefetch_req, i
     const size_t one_per_sm = static_cast<size_t>(per_sm / 2 - reserved + 16);
     if (smem < one_per_sm) smem = one_per_sm;
   }
-  if (g.cluster == 1 && grid <= sm_count()) {
-    // Residency under programmatic dependent launch. When one call fills
-    // every SM, two CTAs per SM (the running call and the next one waiting
-    // on it) let the next call's CTAs start early and spread over the SMs
-    // instead of piling onto the ones this call left room on. When the batch
-    // leaves SMs free, one CTA per SM measured faster: the next call lands
-    // on SMs of its own (64 x 2048: 2.19 -> 1.80 us per call; 128 x 2048:
-    // 2.29 -> 1.87), while at 256 rows on 148 SMs it was slower (2.24 ->
-    // 2.34).
+  if (g.cluster == 1 && grid <= int64_t{4} * sm_count()) {
+    // Residency under programmatic dependent launch: the next call's CTAs
+    // become resident wherever this call leaves room. When the batch leaves
+    // SMs free, one CTA per SM measured faster: the next call lands on SMs
+    // of its own (64 x 2048: 2.19 -> 1.80 us per call; 128 x 2048: 2.29 ->
+    // 1.87). When a call fills the SMs, as many per SM as the call needs
+    // (two for up to two CTAs per SM, and so on), so the next call's CTAs
+    // spread over the SMs instead of piling onto the ones this call left
+    // room on.
     int per_sm = 0, reserved = 0;
     smem_limits(&per_sm, &reserved);
-    const int per_sm_ctas = grid < sm_count() ? 1 : 2;
+    const int per_sm_ctas = grid < sm_count() ? 1 : static_cast<int>((grid + sm_count() - 1) / sm_count());
     const size_t reserve = static_cast<size_t>(per_sm / (per_sm_ctas + 1) - reserved + 16);
     if (smem < reserve) smem = reserve;
   }
