@@ -878,6 +878,11 @@ class ConverterSets:
         return ok
 
 
+def _min_over_ranks(dist, value: int) -> int:
+    """The smallest ``value`` over all ranks."""
+    return int(-reduce_max(dist, -float(value)))
+
+
 def _all_ranks(dist, ok: bool) -> bool:
     """True when ``ok`` holds on every rank."""
     return reduce_max(dist, 0.0 if ok else 1.0) == 0.0
@@ -1071,7 +1076,7 @@ def _replay_gate_sub(rank: int, world: int, dev, dist) -> dict:
     return {
         "workload": WORKLOADS[5]["desc"],
         "layers": len(layers),
-        "replays": int(reduce_max(dist, -gate.replays)) * -1,  # the fewest over ranks
+        "replays": _min_over_ranks(dist, gate.replays),
         "mismatches": int(reduce_max(dist, max(gate.mismatches, 0) if gate.error is None else 1 << 30)),
         "checkpoints": sorted(gate.checkpoints),
         "ok": _all_ranks(dist, gate.ok),
