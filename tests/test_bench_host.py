@@ -1,8 +1,8 @@
 """Host-side logic of the multi-GPU bench, on CPU: gloo ranks, no GPU.
 
 Each rank of ``bench.py`` converts its own DCP rank independently; the only
-cross-process steps are a barrier and a max-reduction of the timed duration.
-Here two gloo processes run exactly those steps.
+cross-process steps are barriers and reductions of the timed durations and
+the checks. Here two gloo processes run exactly those steps.
 """
 
 from __future__ import annotations
@@ -44,8 +44,13 @@ def _worker(rank: int, world: int, port: int, out_path: str) -> None:
         plan = bench.shard_plan(rank, world)
         dist.barrier()
         value = bench.reduce_max(dist, 10.0 * (rank + 1))
+        # the same collective steps, in the same order, on every rank
+        fewest = bench._min_over_ranks(dist, 10_000 - rank)
+        all_ok = bench._all_ranks(dist, rank != 1)
+        all_true = bench._all_ranks(dist, True)
         with open(f"{out_path}.{rank}", "w") as fh:
-            json.dump({"plan": plan, "max": value}, fh)
+            json.dump({"plan": plan, "max": value, "fewest": fewest, "all_ok": all_ok,
+                       "all_true": all_true}, fh)
     finally:
         dist.destroy_process_group()
 
@@ -65,6 +70,23 @@ def test_two_gloo_ranks_barrier_and_max(tmp_path) -> None:
     results = [json.load(open(f"{out}.{r}")) for r in range(2)]
     assert [r["plan"]["dcp_rank"] for r in results] == [0, 1]
     assert all(r["max"] == 20.0 for r in results)
+    assert all(r["fewest"] == 9_999 for r in results)
+    assert all(r["all_ok"] is False and r["all_true"] is True for r in results)
+
+
+def test_traffic_is_used_only_for_the_kernel_source_it_was_captured_from(tmp_path, monkeypatch) -> None:
+    data = {"kernel_sha256": bench.kernel_digest(), "configs": {"3": {"read": 100, "write": 20}}}
+    path = tmp_path / "traffic.json"
+    path.write_text(json.dumps(data))
+    monkeypatch.setattr(bench, "TRAFFIC_FILE", str(path))
+    assert bench._traffic(3)["bytes"] == 120
+    assert bench._traffic(4)["bytes"] is None
+    data["kernel_sha256"] = "0" * 64
+    path.write_text(json.dumps(data))
+    stale = bench._traffic(3)
+    assert stale["bytes"] is None and "predates" in stale["source"]
+    monkeypatch.setattr(bench, "TRAFFIC_FILE", str(tmp_path / "missing.json"))
+    assert bench._traffic(3)["bytes"] is None
 
 
 def test_reference_arm_line_on_cpu() -> None:
