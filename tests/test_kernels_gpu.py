@@ -547,10 +547,11 @@ def test_decode_step_of_48_layers_in_one_graph(golden) -> None:
 
 
 @pytest.mark.parametrize("width", [4, 100, 512, 2048, 6000])
-@pytest.mark.parametrize("batch", [1, 147, 148, 149, 296, 297, 1000, 3000])
+@pytest.mark.parametrize("batch", [1, 147, 148, 149, 296, 297, 591, 592, 593, 887, 888, 1000, 3000])
 def test_row_groups_over_batch_sizes(width, batch) -> None:
-    """Row-wise CTAs pack several rows (up to 512 threads) and spread the batch
-    over at most one CTA per SM; every batch/width split must stay exact."""
+    """Every batch/width split of the row-wise geometry stays exact: one row
+    per CTA up to four rows per SM (592 on 148 SMs), rows packed into CTAs of
+    up to 512 threads beyond, and 16-column runs from six rows per SM (888)."""
     if batch * width > 4_000_000:
         pytest.skip("large case covered by the full-size tests")
     rng = np.random.default_rng(batch * 7 + width)
