@@ -15,8 +15,9 @@
 //      N + 1 therefore reads DRAM while call N is still running;
 //   1. read the request id, the thread's run of tokens (one 256-bit load per
 //      eight columns when the run is 32-byte aligned) and, when the table is
-//      staged, the request's block-table row into shared memory in the same
-//      wave (speculating that row r belongs to request r, repaired when not);
+//      staged (an explicit option; the default gathers from L2), the
+//      request's block-table row into shared memory in the same wave
+//      (speculating that row r belongs to request r, repaired when not);
 //   2. apply ownership and deinterleave: with interleave 1 and powers of two,
 //      one rotate and one unsigned compare decide ownership, sign and table
 //      bounds together; otherwise shifts or invariant-divisor multiplies;
@@ -185,10 +186,10 @@ __host__ __device__ constexpr int count_bits(int g) { return g < 2 ? 1 : 1 + cou
 //
 // Without a cluster a CTA holds p.rows_base or p.rows_base + 1 consecutive
 // rows, one group of p.row_threads threads per row (each group with its own
-// shared-memory region). Spreading the rows over at most one CTA per SM keeps
-// the load even under programmatic dependent launch: the next call's CTAs
-// become resident where this call left room, and with one-row CTAs several of
-// them could pile onto one SM.
+// shared-memory region): one row while the batch is at most four rows per SM,
+// several beyond. The host's shared-memory reservation bounds how many CTAs
+// share an SM, so under programmatic dependent launch the next call's CTAs
+// spread over the SMs instead of piling onto the ones this call left room on.
 template <int G, bool CLUSTER, int MODE, bool COMPACT, bool STAGE>
 __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
     localize_kernel(const __grid_constant__ Params p) {
