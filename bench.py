@@ -91,11 +91,14 @@ KERNEL_SOURCE = os.path.join(REPO, "silkern_b200", "csrc", "localize.cu")
 
 
 def kernel_digest() -> str:
-    """sha256 of the converter kernel's source, which a traffic capture is tied to."""
+    """sha256 of the converter kernel's code (its source without comments or
+    whitespace, so an edited comment keeps a capture current), which a
+    traffic capture is tied to."""
     import hashlib
 
-    with open(KERNEL_SOURCE, "rb") as fh:
-        return hashlib.sha256(fh.read()).hexdigest()
+    with open(KERNEL_SOURCE) as fh:
+        code = re.sub(r"//[^\n]*", "", fh.read())
+    return hashlib.sha256("".join(code.split()).encode()).hexdigest()
 
 
 def _traffic(config: int) -> dict:
