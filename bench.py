@@ -955,6 +955,51 @@ def measure_isolated(sets: ConverterSets, steps: int, warmup: int, dev) -> float
     return (t_with - t_without) / timed
 
 
+# Launch shapes of the copy-floor sweep: (elements per thread, threads per
+# CTA, most CTAs per SM with 0 for no limit).
+COPY_FLOOR_SHAPES = tuple((run, threads, per_sm) for run, threads in
+                          ((8, 128), (8, 256), (8, 512), (8, 1024), (16, 128), (16, 256), (16, 512))
+                          for per_sm in (0, 1, 2, 4))
+
+
+def measure_copy_floor(sets: ConverterSets, steps: int, warmup: int, dev, dist, per_call_s: float) -> dict:
+    """The floor a converter call runs against: each call's tokens copied to
+    its output buffer by silkern_copy_floor_v1 (the converter's loads,
+    stores and launch mode, none of its work), over the same rotating sets,
+    timed like the converter for every launch shape of COPY_FLOOR_SHAPES
+    (max over ranks); the fastest shape is the floor. Overwrites the sets'
+    outputs, so it runs after their check."""
+    import torch
+
+    from silkern_b200.kernels import copy_floor
+
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    shapes = {}
+    for run, threads, per_sm in COPY_FLOOR_SHAPES:
+        def launch(i: int, run=run, threads=threads, per_sm=per_sm) -> None:
+            bufs, _ = sets.sets[i % sets.n_sets]
+            copy_floor(bufs["tokens"], bufs["out"], run=run, threads=threads, ctas_per_sm=per_sm)
+
+        seconds = _replay_seconds(launch, max(3, warmup) * sets.calls, steps * sets.calls, stream, dev)
+        shapes[f"{run}x{threads}/{per_sm}"] = reduce_max(dist, seconds) / (steps * sets.calls) * 1e6
+    best = min(shapes, key=shapes.get)
+    floor_us = shapes[best]
+    moved = 2 * 4 * sum(int(b["tokens"].numel()) for b, _ in sets.sets[:sets.calls]) / sets.calls
+    return {
+        "us_per_call": floor_us,
+        "shape": best,
+        "bytes_per_call": int(moved),
+        "gbs": moved / floor_us / 1e3,
+        "frac_of_peak": moved / floor_us / 1e3 / _peaks()["hbm_gbs"],
+        "converter_frac_of_floor": floor_us / (per_call_s * 1e6),
+        "us_per_call_by_shape": shapes,
+        "what": "tokens copied to out (the converter's loads, stores and launch mode, none of its work), "
+                "back to back over the same rotating sets; fastest of the launch shapes (elements per thread "
+                "x threads per CTA / most CTAs per SM, 0 for no limit)",
+    }
+
+
 def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     import torch
 
@@ -975,6 +1020,9 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
     n_sets = sets.n_sets
     headline_cases = sets.cases[:calls]
 
+    floor = None
+    if impl == "ours":
+        floor = measure_copy_floor(sets, args.steps, args.warmup, dev, dist, per_call_s)
     isolated = None
     if impl == "ours" and world == 1 and args.rows == 0:
         isolated = measure_isolated(sets, min(args.steps, 200), args.warmup, dev)
@@ -1051,6 +1099,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
             "timing": "CUDA events recorded inside the replayed graphs around the timed calls, per call",
         },
         "isolated_us_per_call": None if isolated is None else isolated * 1e6,
+        "copy_floor": floor,
         "gpu_launches": args.steps * calls,
         **extra,
         "e2e": e2e,

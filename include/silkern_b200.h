@@ -25,7 +25,9 @@
  *     previous grid in the stream before it reads any input;
  *   - `status` may be NULL; otherwise a row whose request id is outside
  *     [0, table_rows) is emitted as all -1 with count 0 and the kernel stores
- *     SILKERN_STATUS_BAD_REQUEST into *status (it never clears it);
+ *     SILKERN_STATUS_BAD_REQUEST into *status, and a cluster whose count
+ *     exchange ran out of its wait bound ORs in SILKERN_STATUS_EXCHANGE_TIMEOUT
+ *     (the kernel never clears *status);
  *   - return value: 0 on success, a positive SILKERN_E* code when an argument
  *     is rejected before launch (nothing is enqueued), or -(cudaError_t) when
  *     the launch itself fails.
@@ -52,6 +54,12 @@ extern "C" {
 #define SILKERN_E_SCRATCH 8      /* batch x tiles exceeds SILKERN_NOALLOC_MAX_TILES */
 
 #define SILKERN_STATUS_BAD_REQUEST 1
+/* Status bit of the converter entry points (OR-ed into *status): a row split
+ * over a thread-block cluster whose CTAs did not complete their count
+ * exchange within the kernel's wait bound. The CTAs that gave up store
+ * nothing for that row (out, counts and tiles keep their previous contents).
+ * It does not occur in a working cluster launch. */
+#define SILKERN_STATUS_EXCHANGE_TIMEOUT 4
 /* Status bit of the fused top-k entry point (OR-ed into *status). */
 #define SILKERN_STATUS_BAD_LENGTH 2 /* a seq_len outside [0, logits_width]; clamped */
 
@@ -183,6 +191,22 @@ int silkern_count_mismatches_v1(const int32_t* a, const int32_t* b, int64_t n,
  */
 int silkern_count_segment_mismatches_v1(const int32_t* a, const int32_t* b, int64_t segments,
                                         int64_t segment_elems, int32_t* counters, void* stream);
+
+/*
+ * Measurement reference, not the product: dst[0..n) = src[0..n) (int32) with
+ * the converter's data movement and launch mode and none of its work. CTAs of
+ * `threads` threads (a multiple of 32, at most 1024) each copy a contiguous
+ * chunk of threads * run elements, each thread a run of `run` (8 or 16)
+ * elements with 256-bit accesses where aligned; programmatic dependent launch,
+ * with a bulk L2 prefetch of the chunk issued before the wait on the previous
+ * grid. ctas_per_sm in 1..8 reserves shared memory so that at most that many
+ * of these CTAs share an SM (the converter's residency control); 0 reserves
+ * none. The time of back-to-back calls over the converter's tokens and output
+ * is the floor a converter call of the same size runs against. src and dst
+ * must not overlap (SILKERN_E_ALIAS). No counterpart in the reference.
+ */
+int silkern_copy_floor_v1(const int32_t* src, int32_t* dst, int64_t n, int32_t run, int32_t threads,
+                          int32_t ctas_per_sm, void* stream);
 
 /*
  * Comparison baseline, not the product: the atomic-reservation converter of

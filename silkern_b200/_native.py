@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "silkern_count_mismatches_v1": (_i32, [_ptr, _ptr, _i64, _ptr, _ptr]),
     "silkern_count_segment_mismatches_v1": (_i32, [_ptr, _ptr, _i64, _i64, _ptr, _ptr]),
+    "silkern_copy_floor_v1": (_i32, [_ptr, _ptr, _i64, _i32, _i32, _i32, _ptr]),
     "silkern_atomic_baseline_v1": (
         _i32,
         [_ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i32, _i32, _i32, _i32, _ptr],

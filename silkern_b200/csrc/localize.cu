@@ -24,9 +24,10 @@
 //   3. stable compaction: each thread counts its valid elements, ballots over
 //      the count's bits give each thread its exclusive prefix in the warp,
 //      warp totals go through shared memory and one redux.sync gives each
-//      warp its base; across a cluster, each CTA pushes its total into every
-//      CTA's shared memory (DSMEM) before one cluster barrier. No atomics, so
-//      the order is the selector's order on every run;
+//      warp its base; across a cluster, each CTA stores its total into every
+//      CTA's shared memory (DSMEM, st.async) and each CTA waits, with a bound,
+//      on its own transaction barrier for all of them. No atomics, so the
+//      order is the selector's order on every run;
 //   4. paged translation: each valid element reads its block from the staged
 //      table row (or, unstaged, from the L2 gather issued in step 2);
 //   5. a row that is one CTA's is staged in shared memory at its final
@@ -52,6 +53,10 @@ namespace silkern {
 
 constexpr int kMaxThreads = 512;      // threads per CTA (row groups, or one cluster slice)
 constexpr int kMaxCluster = 8;
+// Polls of a CTA's count-exchange barrier before it gives up (each poll may
+// suspend the thread for a while); the exchange completes within a few
+// microseconds, so only a broken cluster ever reaches the bound.
+constexpr uint32_t kExchangePolls = 1u << 16;
 constexpr int kTableStageMax = 4096;  // block-table entries staged in shared memory
 constexpr int kSmemMax = 200 * 1024;      // dynamic shared memory per CTA, any launch
 constexpr uint32_t kFull = 0xffffffffu;
@@ -197,6 +202,7 @@ __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
   // per row group: [staged table row][staged output][warp totals][tile offsets]
   extern __shared__ __align__(16) int32_t smem[];
   __shared__ int32_t s_cta_total[kMaxCluster];
+  __shared__ __align__(8) uint64_t s_xbar;  // the cluster's count exchange
 
   int nthreads, tid, group;
   int64_t row;
@@ -209,7 +215,13 @@ __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
     row = cluster_id_x();
     crank = static_cast<int>(cluster_ctarank());
     active = true;
-    cluster_arrive_relaxed();  // phase 0: this CTA is resident
+    if (threadIdx.x == 0) {
+      // Completes when this thread has arrived and 4 bytes (one CTA total)
+      // have landed from every CTA of the cluster, this one included.
+      mbar_init_cluster(&s_xbar, 1);
+      mbar_arrive_expect_tx(&s_xbar, 4u * static_cast<uint32_t>(p.cluster));
+    }
+    cluster_arrive_relaxed();  // phase 0: this CTA is resident, its barrier initialised
   } else {
     nthreads = p.row_threads;
     group = static_cast<int>(threadIdx.x >> p.row_threads_shift);
@@ -330,14 +342,31 @@ __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
   const int pos = __reduce_add_sync(kFull, lane < warp ? x : 0) + excl;
   const int cta_total = __reduce_add_sync(kFull, x);
 
+  // Hierarchical: the CTA-local exclusive position of each tile's first
+  // column is that tile's offset (before the row offset). Tiles are
+  // multiples of 64 columns and G divides 64, so every tile starts at some
+  // thread's first column.
+  const bool tiles = p.tile_shift >= 0;
+  if (tiles && col < len && (col & ((1 << p.tile_shift) - 1)) == 0) s_tile[col >> p.tile_shift] = pos;
+
   int row_off = 0;
   int row_total = cta_total;
   if constexpr (CLUSTER) {
     const int cs = p.cluster;
-    cluster_wait_acquire();  // phase 0 complete: every CTA of the cluster runs
-    if (tid < cs) st_shared_cluster(&s_cta_total[crank], static_cast<uint32_t>(tid), cta_total);
-    cluster_arrive_release();
-    cluster_wait_acquire();  // phase 1: every CTA's total is in s_cta_total
+    // The last CTA barrier of a cluster CTA: after the exchange below a
+    // thread may leave on its own.
+    if (tiles) __syncthreads();  // s_tile is complete
+    cluster_wait_acquire();  // phase 0 complete: every CTA runs, every barrier is initialised
+    // Push this CTA's total into every CTA's s_cta_total[crank]. The store
+    // completes a transaction on the receiver's barrier, so no release fence
+    // or second cluster barrier is needed. No CTA exits before all totals
+    // have reached it, and no CTA writes another's shared memory after that.
+    if (tid < cs) st_async_cluster(&s_cta_total[crank], &s_xbar, static_cast<uint32_t>(tid), cta_total);
+    if (!mbar_wait_cluster(&s_xbar, 0, kExchangePolls)) {
+      // Only a broken cluster gets here: store nothing for the row.
+      if (p.status != nullptr) atomicOr(p.status, SILKERN_STATUS_EXCHANGE_TIMEOUT);
+      return;
+    }
     row_total = 0;
     for (int r = 0; r < cs; ++r) {
       const int w = s_cta_total[r];
@@ -371,13 +400,6 @@ __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
     // A compacting call never stores an invalid element: no select needed.
     v[j] = (COMPACT || ((bits >> j) & 1u)) ? phys : -1;
   }
-
-  // Hierarchical: the CTA-local exclusive position of each tile's first
-  // column is that tile's offset (before the row offset). Tiles are
-  // multiples of 64 columns and G divides 64, so every tile starts at some
-  // thread's first column.
-  const bool tiles = p.tile_shift >= 0;
-  if (tiles && col < len && (col & ((1 << p.tile_shift) - 1)) == 0) s_tile[col >> p.tile_shift] = pos;
 
   int32_t* orow = p.out + row * p.width;
   if constexpr (COMPACT && !CLUSTER) {
@@ -422,9 +444,8 @@ __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
       k += static_cast<int>((bits >> j) & 1u);
     }
     fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
-    if (tiles) __syncthreads();  // s_tile is complete
   } else {
-    if (tiles) __syncthreads();  // s_tile is complete
+    if (tiles && !CLUSTER) __syncthreads();  // s_tile is complete (a cluster CTA's already was)
     if (col < len) store_run<G>(orow + c0 + col, len - col, v);
   }
 
@@ -449,6 +470,32 @@ __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
 // calls. Host code must not pass this symbol to a kernel: its device address
 // comes from cudaGetSymbolAddress (noalloc_scratch below).
 static __device__ __align__(256) int32_t g_noalloc_tiles[2 * SILKERN_NOALLOC_MAX_TILES];
+
+// The converter's data movement without its work: dst = src, each CTA a
+// contiguous chunk of blockDim.x * G elements, each thread a run of G, with
+// the converter's launch mode (programmatic dependent launch, a bulk L2
+// prefetch of the chunk before the wait) and its run loads and stores. The
+// time of a call is the floor a converter call of the same bytes moves
+// against.
+template <int G>
+__global__ void __launch_bounds__(1024) copy_floor_kernel(const int32_t* src, int32_t* dst, int64_t n) {
+  pdl_launch_dependents();
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * blockDim.x * G;
+  const int64_t left = n - c0;
+  const int len = left < static_cast<int64_t>(blockDim.x) * G ? static_cast<int>(left) : blockDim.x * G;
+  if (threadIdx.x == 0) {
+    const uintptr_t lo = (reinterpret_cast<uintptr_t>(src + c0) + 15u) & ~uintptr_t{15};
+    const uintptr_t hi = reinterpret_cast<uintptr_t>(src + c0 + len) & ~uintptr_t{15};
+    if (hi > lo) prefetch_l2_bulk(reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo));
+  }
+  pdl_wait();
+  const int col = static_cast<int>(threadIdx.x) * G;
+  if (col < len) {
+    int32_t v[G];
+    load_run<G>(src + c0 + col, len - col, v);
+    store_run<G>(dst + c0 + col, len - col, v);
+  }
+}
 
 // Adds the number of differing positions to *mismatches.
 __global__ void __launch_bounds__(256) count_mismatches_kernel(const int32_t* a, const int32_t* b,
@@ -1143,6 +1190,54 @@ extern "C" int silkern_count_mismatches_v1(const int32_t* a, const int32_t* b, i
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, silkern::count_mismatches_kernel, a, b, n, mismatches);
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -static_cast<int>(err);
+  }
+  return SILKERN_OK;
+}
+
+extern "C" int silkern_copy_floor_v1(const int32_t* src, int32_t* dst, int64_t n, int32_t run,
+                                     int32_t threads, int32_t ctas_per_sm, void* stream) {
+  if (!src || !dst) return SILKERN_E_NULL;
+  if (n < 0) return SILKERN_E_SHAPE;
+  if ((run != 8 && run != 16) || threads < 32 || threads > 1024 || threads % 32 != 0 || ctas_per_sm < 0 ||
+      ctas_per_sm > 8) {
+    return SILKERN_E_GEOMETRY;
+  }
+  if (silkern::overlaps(src, n, dst, n)) return SILKERN_E_ALIAS;
+  if (n == 0) return SILKERN_OK;
+  const int64_t per_cta = static_cast<int64_t>(threads) * run;
+  const int64_t blocks = (n + per_cta - 1) / per_cta;
+  if (blocks > INT32_MAX) return SILKERN_E_SHAPE;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  void (*fn)(const int32_t*, int32_t*, int64_t) =
+      run == 8 ? silkern::copy_floor_kernel<8> : silkern::copy_floor_kernel<16>;
+  if (ctas_per_sm > 0) {
+    // The converter's residency control: a shared-memory reservation that
+    // lets at most ctas_per_sm of these CTAs share an SM, so the next call's
+    // CTAs (launched early under programmatic dependent launch) spread out.
+    int per_sm = 0, reserved = 0;
+    silkern::smem_limits(&per_sm, &reserved);
+    cfg.dynamicSmemBytes = static_cast<size_t>(per_sm / (ctas_per_sm + 1) - reserved + 16);
+    if (cfg.dynamicSmemBytes > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(cfg.dynamicSmemBytes));
+      if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return -static_cast<int>(e);
+      }
+    }
+  }
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, fn, src, dst, n);
   if (err != cudaSuccess) {
     (void)cudaGetLastError();
     return -static_cast<int>(err);

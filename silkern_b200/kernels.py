@@ -145,7 +145,11 @@ def localize_rowwise(
     interface compatibility (4 or 8); the launch geometry is chosen by the
     library. ``status`` (optional, one int32 element) receives
     ``SILKERN_STATUS_BAD_REQUEST`` if a request id is outside the block table;
-    such a row is emitted as all ``-1`` with count 0.
+    such a row is emitted as all ``-1`` with count 0. A row split over a
+    thread-block cluster (rows wider than 8192 columns, few rows) whose count
+    exchange runs out of its wait bound ORs in
+    ``SILKERN_STATUS_EXCHANGE_TIMEOUT`` (4); the CTAs that gave up store
+    nothing for it.
 
     Under ``torch.compile`` the call is the custom op
     ``torch.ops.silkern_b200.localize_rowwise`` (one opaque node, checked and
@@ -470,6 +474,28 @@ def count_segment_mismatches(a, b, counters) -> None:
             a.data_ptr(), b.data_ptr(), segments, a.numel() // max(segments, 1), counters.data_ptr(), stream
         )
     _native.check(code, "count_segment_mismatches")
+
+
+def copy_floor(src, dst, *, run: int = 8, threads: int = 256, ctas_per_sm: int = 0) -> None:
+    """``dst.copy_(src)`` (int32, contiguous, same number of elements) with the
+    converter's data movement and launch mode and none of its work: the floor
+    a converter call over the same bytes is measured against. CTAs of
+    ``threads`` threads, each thread a run of ``run`` (8 or 16) elements; with
+    ``ctas_per_sm`` (1-8) at most that many CTAs share an SM (0: no limit).
+    Capturable in a CUDA graph.
+    """
+    import torch
+
+    if src.dtype != torch.int32 or dst.dtype != torch.int32 or src.numel() != dst.numel():
+        raise LocalizationError("copy_floor needs two int32 tensors with the same number of elements")
+    if not (src.is_contiguous() and dst.is_contiguous()):
+        raise LocalizationError("copy_floor needs contiguous tensors")
+    lib = _native.load()
+    with _device_scope(torch, src.device):
+        stream = torch.cuda.current_stream(src.device).cuda_stream
+        code = lib.silkern_copy_floor_v1(src.data_ptr(), dst.data_ptr(), src.numel(), int(run), int(threads),
+                                         int(ctas_per_sm), stream)
+    _native.check(code, "copy_floor")
 
 
 if "torch" in sys.modules:  # torch is already loaded: define the ops now (see silkern_b200.ops)

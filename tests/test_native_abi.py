@@ -171,6 +171,20 @@ def test_segment_mismatch_counter_rejects(lib) -> None:
     assert call(OUT, TOK, 0, 16, CNT, None) == 0  # nothing to compare: no launch
 
 
+def test_copy_floor_rejects(lib) -> None:
+    call = lib.silkern_copy_floor_v1
+    assert call(None, OUT, 16, 8, 256, 0, None) == 1
+    assert call(TOK, None, 16, 8, 256, 0, None) == 1
+    assert call(TOK, OUT, -1, 8, 256, 0, None) == 2
+    assert call(TOK, OUT, 16, 4, 256, 0, None) == 7
+    assert call(TOK, OUT, 16, 8, 48, 0, None) == 7
+    assert call(TOK, OUT, 16, 8, 2048, 0, None) == 7
+    assert call(TOK, OUT, 16, 8, 256, -1, None) == 7
+    assert call(TOK, OUT, 16, 8, 256, 9, None) == 7
+    assert call(TOK, TOK + 32, 16, 8, 256, 0, None) == 6
+    assert call(TOK, OUT, 0, 8, 256, 2, None) == 0  # nothing to copy: no launch
+
+
 def test_explicit_rejects_bad_geometry(lib) -> None:
     def call(cluster, stage=-1, prefetch=-1, width=16, chunks=0):
         return lib.silkern_localize_explicit_v1(
