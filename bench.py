@@ -921,6 +921,11 @@ def measure_converter(sets: ConverterSets, steps: int, warmup: int, dev, dist=No
     return {"per_step_s": per_step_s, "per_call_s": per_step_s / sets.calls, "bit_exact": ok}
 
 
+# Calls per timing of isolated_us_per_call, whatever --steps is: the figure
+# is the difference of two timings, which 20 calls leave noisy.
+ISOLATED_CALLS = 200
+
+
 def measure_isolated(sets: ConverterSets, steps: int, warmup: int, dev) -> float:
     """Seconds one converter call adds between a producer kernel that writes
     its tokens and a consumer kernel that reads its output, with no other
@@ -950,9 +955,10 @@ def measure_isolated(sets: ConverterSets, steps: int, warmup: int, dev) -> float
     stream.wait_stream(torch.cuda.current_stream(dev))
     warm = max(3, warmup) * sets.calls
     timed = steps * sets.calls
-    t_with = _replay_seconds(with_call, warm, timed, stream, dev)
-    t_without = _replay_seconds(without_call, warm, timed, stream, dev)
-    return (t_with - t_without) / timed
+    # Median of three alternating pairs.
+    diffs = sorted(_replay_seconds(with_call, warm, timed, stream, dev) -
+                   _replay_seconds(without_call, warm, timed, stream, dev) for _ in range(3))
+    return diffs[1] / timed
 
 
 # Launch shapes of the copy-floor sweep: (elements per thread, threads per
@@ -1025,7 +1031,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> dict | None:
         floor = measure_copy_floor(sets, args.steps, args.warmup, dev, dist, per_call_s)
     isolated = None
     if impl == "ours" and world == 1 and args.rows == 0:
-        isolated = measure_isolated(sets, min(args.steps, 200), args.warmup, dev)
+        isolated = measure_isolated(sets, ISOLATED_CALLS, args.warmup, dev)
     del sets
     torch.cuda.empty_cache()
 
@@ -1149,7 +1155,7 @@ def _triton_sub(config: int, args, dev) -> dict:
     try:
         sets = ConverterSets(config, shard_plan(0, 1, config), dev, impl="triton", ref_silkern=ref_silkern)
         t = measure_converter(sets, args.steps, args.warmup, dev)
-        isolated = measure_isolated(sets, min(args.steps, 200), args.warmup, dev)
+        isolated = measure_isolated(sets, ISOLATED_CALLS, args.warmup, dev)
     except Exception as exc:  # the comparison arm must not take the headline down
         return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
     finally:
