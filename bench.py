@@ -1180,17 +1180,30 @@ def _stack_rows(case, rows: int):
                                tokens=np.ascontiguousarray(np.tile(case.tokens, (reps, 1))[:rows]))
 
 
+# End-to-end steps when --e2e-steps is not given, at least: the step is bound
+# by the host link, and 20 steps over a few streams are mostly the pipeline's
+# fill and drain (one box: 132.8 us per step over 20 steps on 4 streams, 59.3
+# over 200).
+E2E_MIN_STEPS = 200
+# Pinned host bytes the end-to-end lanes may hold in all (each lane has its
+# own inputs and outputs).
+E2E_LANE_BYTES = 1 << 30
+
+
 def run_e2e(args, cases, dev, dist) -> dict:
     """Same metric through the public API, host inputs in and results out every step."""
     import torch
 
     from silkern_b200.workspace import workspace_shapes
 
-    steps = args.e2e_steps if args.e2e_steps > 0 else args.steps
+    steps = args.e2e_steps if args.e2e_steps > 0 else max(args.steps, E2E_MIN_STEPS)
     arm = WORKLOADS[args.config]["arm"]
     lanes = []
     h2d = d2h = 0
-    n_lanes = max(1, args.e2e_lanes)
+    # Every lane holds its own pinned and device copy of a step's buffers:
+    # at most E2E_LANE_BYTES of them in all.
+    lane_bytes = sum(4 * (c.req_ids.size + c.block_table.size + 2 * c.tokens.size + c.batch) for c in cases)
+    n_lanes = max(1, min(args.e2e_lanes, E2E_LANE_BYTES // max(1, lane_bytes)))
     for lane_index in range(n_lanes):
         stream = torch.cuda.Stream(device=dev)
         jobs = []
@@ -1336,12 +1349,13 @@ def main(argv=None) -> int:
     parser.add_argument("--impl", choices=["ours", "reference", "triton", "vllm", "fused", "atomic", "link"],
                         default="ours")
     parser.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=3)
-    parser.add_argument("--e2e-steps", type=int, default=0, help="end-to-end steps (default: --steps)")
+    parser.add_argument("--e2e-steps", type=int, default=0,
+                        help=f"end-to-end steps (default: --steps, at least {E2E_MIN_STEPS})")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--batch", type=int, default=0, help="rows of the fused arm (default 256)")
     parser.add_argument("--rows", type=int, default=0,
                         help="rows per converter call: the workload's rows repeated (default: its own batch)")
-    parser.add_argument("--e2e-lanes", type=int, default=4,
+    parser.add_argument("--e2e-lanes", type=int, default=8,
                         help="streams the end-to-end steps alternate over, each with its own buffers")
     parser.add_argument("--headline-only", action="store_true",
                         help="skip the other workloads, the Triton comparison and the replay gate")

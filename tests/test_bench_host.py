@@ -159,4 +159,4 @@ def test_cli_accepts_the_sizing_and_lane_options() -> None:
             bench.main([])
     finally:
         argparse.ArgumentParser.parse_args = original
-    assert seen["impl"] == "ours" and seen["rows"] == 0 and seen["e2e_lanes"] == 4 and seen["config"] == 3
+    assert seen["impl"] == "ours" and seen["rows"] == 0 and seen["e2e_lanes"] == 8 and seen["config"] == 3
