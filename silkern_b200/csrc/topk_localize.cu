@@ -99,6 +99,10 @@ struct TopkParams {
   int32_t block_size;
   FastDiv div_il, div_dcp, div_bs;
   int32_t pow2;  // interleave, dcp_size and block_size all powers of two: shifts below
+  // Start the row streaming into L2 before waiting on the previous grid
+  // (batches of at least half an SM count per SM; below that the rows'
+  // phases, not their bytes, set a call's time).
+  int32_t early_prefetch;
   uint32_t il_shift, dcp_shift, bs_shift;
   // dynamic shared memory layout (byte offsets, 16-byte aligned)
   int32_t off_boff, off_key, off_pos, off_table;
@@ -329,6 +333,25 @@ __global__ void __launch_bounds__(T, T == kSmallCta ? 2 : 1)
   const uint32_t lt = lanemask_lt();
   const int64_t row = blockIdx.x;
   pdl_launch_dependents();
+  int hint = -1;
+  if (p.early_prefetch) {
+    // The row's length as it stands before the previous grid is done, read
+    // through L2 only (no copy of a value that grid may still write stays in
+    // L1): a hint to start the row streaming into L2 while that grid
+    // finishes. A prefetch only fills L2, the device's point of coherence, so
+    // it never makes a later load stale.
+    hint = __ldcg(p.seq_lens + row);
+    hint = hint < 0 ? 0 : (hint > p.width ? p.width : hint);
+    if (hint > p.k && p.vec) {
+      const int64_t bytes = static_cast<int64_t>(hint & ~3) * 4;
+      const float* base = p.logits + row * p.stride;
+      for (int64_t off = static_cast<int64_t>(threadIdx.x) * kPrefetchBytes; off < bytes;
+           off += static_cast<int64_t>(T) * kPrefetchBytes) {
+        const int64_t m = bytes - off < kPrefetchBytes ? bytes - off : kPrefetchBytes;
+        prefetch_l2_bulk(base + off / 4, static_cast<uint32_t>(m));
+      }
+    }
+  }
   pdl_wait();  // everything below may read what the previous grid wrote
 
   int len = __ldg(p.seq_lens + row);
@@ -379,9 +402,9 @@ __global__ void __launch_bounds__(T, T == kSmallCta ? 2 : 1)
     if (4 * g0 < len) first[0] = sample(g0);
     if (4 * g1 < len) first[1] = sample(g1);
   }
-  if (len > k && vec) {
-    // Start the whole row streaming into L2 now; the stream pass below then
-    // mostly hits L2.
+  if (len > k && vec && len != hint) {
+    // Start the whole row streaming into L2 now (unless the early prefetch
+    // above already did); the stream pass below then mostly hits L2.
     const int64_t bytes = static_cast<int64_t>(len & ~3) * 4;
     for (int64_t off = static_cast<int64_t>(tid) * kPrefetchBytes; off < bytes;
          off += static_cast<int64_t>(kTopkThreads) * kPrefetchBytes) {
@@ -859,6 +882,10 @@ int topk_launch(const float* logits, int64_t stride, int64_t width, const int32_
             pow2_shift(static_cast<uint32_t>(block_size), &p.bs_shift))
                ? 1
                : 0;
+  // Early prefetch from half a row per SM: 256 rows of up to 65536 scores
+  // measured 28.5 -> 25.3 us per call, 148 rows 17.9 -> 16.4; at 64 rows
+  // and below it was slower (64 rows: 16.9 against 16.3).
+  p.early_prefetch = 2 * batch >= static_cast<int64_t>(sms) ? 1 : 0;
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(batch), 1, 1);
