@@ -338,8 +338,10 @@ __global__ void __launch_bounds__(T, T == kSmallCta ? 2 : 1)
     // The row's length as it stands before the previous grid is done, read
     // through L2 only (no copy of a value that grid may still write stays in
     // L1): a hint to start the row streaming into L2 while that grid
-    // finishes. A prefetch only fills L2, the device's point of coherence, so
-    // it never makes a later load stale.
+    // finishes. Whatever it reads (that grid may be writing it) is clamped to
+    // the row and only bounds the prefetch; the length used below is read
+    // after the wait. A prefetch only fills L2, the device's point of
+    // coherence, so it never makes a later load stale.
     hint = __ldcg(p.seq_lens + row);
     hint = hint < 0 ? 0 : (hint > p.width ? p.width : hint);
     if (hint > p.k && p.vec) {
