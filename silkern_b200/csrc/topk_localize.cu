@@ -354,6 +354,12 @@ __global__ void __launch_bounds__(T, T == kSmallCta ? 2 : 1)
       }
     }
   }
+  // Shared memory only, so it runs while the previous grid finishes: clear
+  // both histograms (1 row: 14.90 -> 14.43 us per call; 256 rows 25.37 ->
+  // 25.0).
+  zero_hist<T>(s_hist[0], tid);
+  zero_hist<T>(s_hist[1], tid);
+  __syncthreads();
   pdl_wait();  // everything below may read what the previous grid wrote
 
   int len = __ldg(p.seq_lens + row);
@@ -428,10 +434,8 @@ __global__ void __launch_bounds__(T, T == kSmallCta ? 2 : 1)
   bool all_selected = true;
 
   if (len > k) {
-    // 1. estimate from every 16th float4
-    zero_hist<T>(s_hist[0], tid);
-    zero_hist<T>(s_hist[1], tid);
-    __syncthreads();
+    // 1. estimate from every 16th float4 (both histograms were cleared
+    // before the wait)
     uint32_t lo_bin = 0u;
     if (sampled) {
       auto count = [&](const float4& v) {
