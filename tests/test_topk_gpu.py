@@ -308,6 +308,68 @@ def test_graph_replay_is_bitwise_stable() -> None:
     assert torch.cuda.memory_allocated() == allocated
 
 
+@pytest.mark.parametrize("kind", ["normal", "ties"])
+@pytest.mark.parametrize("above_sm_count", [False, True])
+def test_batches_from_half_the_sms_match_oracle(kind, above_sm_count) -> None:
+    """From half a row per SM each CTA starts its row streaming into L2 before
+    it waits on the previous grid (1024-thread CTAs up to the SM count,
+    512-thread ones above it); those batches match the oracle too."""
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    batch = sms + 12 if above_sm_count else sms // 2 + 3
+    width, top_k = 4096, 256
+    rng = np.random.default_rng(9100 + 2 * KINDS.index(kind) + int(above_sm_count))
+    logits = _values(rng, kind, (batch, width))
+    lens = _lens(rng, batch, width, top_k)
+    table = _table(rng, 11, 1 + width // 64)
+    req = rng.integers(0, 11, size=batch).astype(np.int32)
+    geometry = dict(block_size=64, dcp_size=4, dcp_rank=1)
+    pos, out, counts = _run(_dev(logits), lens, req, table, top_k, **geometry)
+    want = oracle_topk(logits, lens, req, table, top_k=top_k, threads=8, **geometry)
+    assert np.array_equal(pos, want[0]) and np.array_equal(out, want[1]) and np.array_equal(counts, want[2])
+
+
+def test_row_lengths_written_by_the_previous_grid() -> None:
+    """The length the kernel reads before waiting on the previous grid is only
+    a prefetch hint: here the previous grid (a converter call, which lets its
+    dependents start at once) is still writing the lengths. Its counts are the
+    top-k's row lengths, back to back in one stream, after each round resets
+    them to a value past the row; every round matches the oracle on the final
+    lengths."""
+    import oracle
+
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    batch, conv_width, top_k = sms + 12, 2048, 128
+    rng = np.random.default_rng(9200)
+    conv_geometry = dict(block_size=64, dcp_size=2, dcp_rank=0)
+    conv_req = np.arange(batch, dtype=np.int32)
+    conv_table = rng.integers(0, 1 << 16, size=(batch, 64)).astype(np.int32)
+    tokens = rng.integers(-1, 8192, size=(batch, conv_width)).astype(np.int32)
+    _, lens = oracle.localize(conv_req, conv_table, tokens, **conv_geometry)
+    assert lens.min() > top_k and lens.max() <= conv_width  # rows past top_k: the sampled path
+
+    logits = rng.standard_normal((batch, conv_width)).astype(np.float32)
+    table = _table(rng, 7, 1 + conv_width // 64)
+    req = rng.integers(0, 7, size=batch).astype(np.int32)
+    geometry = dict(block_size=64, dcp_size=4, dcp_rank=2)
+    want = oracle_topk(logits, lens, req, table, top_k=top_k, threads=8, **geometry)
+
+    conv_in = [_dev(a) for a in (conv_req, conv_table, tokens)]
+    conv_out = torch.empty((batch, conv_width), dtype=torch.int32, device=DEV)
+    seq_lens = torch.empty(batch, dtype=torch.int32, device=DEV)
+    logits_t, req_t, table_t = _dev(logits), _dev(req), _dev(table)
+    for _ in range(4):
+        out = torch.full((batch, top_k), 0x5A5A5A5A, dtype=torch.int32, device=DEV)
+        counts = torch.full((batch,), 0x5A5A5A5A, dtype=torch.int32, device=DEV)
+        pos = torch.full((batch, top_k), 0x5A5A5A5A, dtype=torch.int32, device=DEV)
+        seq_lens.fill_(5 * conv_width)  # past the row until the converter writes it
+        localize_rowwise(*conv_in, conv_out, seq_lens, **conv_geometry)
+        topk_localize(logits_t, seq_lens, req_t, table_t, out, counts, positions=pos, **geometry)
+        torch.cuda.synchronize()
+        assert np.array_equal(seq_lens.cpu().numpy(), lens)
+        assert np.array_equal(pos.cpu().numpy(), want[0])
+        assert np.array_equal(out.cpu().numpy(), want[1]) and np.array_equal(counts.cpu().numpy(), want[2])
+
+
 def test_matches_vllm_radix_topk_then_converter() -> None:
     """vLLM's decode top-k (``torch.ops._C.persistent_topk``) selects the same sets.
 
