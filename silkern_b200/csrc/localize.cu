@@ -102,21 +102,6 @@ struct Params {
   uint32_t il_mask, dcp_mask, bs_mask;
 };
 
-// out[lo:hi] = -1 with 128-bit stores on the aligned body.
-__device__ __forceinline__ void fill_invalid(int32_t* row, int lo, int hi, int tid, int nthreads) {
-  if (lo >= hi) return;
-  int32_t* dst = row + lo;
-  const int n = hi - lo;
-  int head = static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 2);
-  head = head < n ? head : n;
-  if (tid < head) dst[tid] = -1;
-  const int nvec = (n - head) >> 2;
-  int4* body = reinterpret_cast<int4*>(dst + head);
-  for (int g = tid; g < nvec; g += nthreads) body[g] = make_int4(-1, -1, -1, -1);
-  const int rest = n - head - 4 * nvec;
-  if (tid < rest) dst[head + 4 * nvec + tid] = -1;
-}
-
 // v[0..G) = src[0..n) and -1 past n (n may be <= 0): 256-bit loads when the
 // run is whole and 32-byte aligned, 128-bit when 16-byte aligned, else scalar.
 template <int G>
@@ -435,7 +420,7 @@ __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
     }
   } else if constexpr (COMPACT) {
     // Across a cluster each survivor goes straight to its final position
-    // after the CTA's row offset; then the -1 tail of the CTA's own slice.
+    // after the CTA's row offset; then the -1 tail within the CTA's own slice.
     int32_t* dst = orow + row_off + pos;
     int k = 0;
 #pragma unroll
@@ -443,7 +428,25 @@ __global__ void __launch_bounds__(kMaxThreads, (CLUSTER || G > 16) ? 1 : 2)
       if ((bits >> j) & 1u) dst[k] = v[j];
       k += static_cast<int>((bits >> j) & 1u);
     }
-    fill_invalid(orow, row_total > c0 ? row_total : c0, c0 + len, tid, nthreads);
+    // The -1 tail: each thread writes its own run of columns where it lies
+    // past the row's count (positions below the count get survivors, from
+    // whichever CTA holds them). One 256-bit store per run instead of a
+    // strided fill of the slice: config 4 took 2.80 against 3.00 us per call.
+    if (col < len) {
+      const int g0 = c0 + col;
+      const int n = len - col < G ? len - col : G;
+      if (g0 >= row_total) {
+        int32_t w[G];
+#pragma unroll
+        for (int j = 0; j < G; ++j) w[j] = -1;
+        store_run<G>(orow + g0, n, w);
+      } else if (g0 + n > row_total) {
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          if (j < n && g0 + j >= row_total) orow[g0 + j] = -1;
+        }
+      }
+    }
   } else {
     if (tiles && !CLUSTER) __syncthreads();  // s_tile is complete (a cluster CTA's already was)
     if (col < len) store_run<G>(orow + c0 + col, len - col, v);
