@@ -274,6 +274,10 @@ def _cpu_baseline(config: int, threads: int, seconds: float = 10.0) -> dict:
     }
 
 
+# Seconds the reference arm's timed steps take in all, whatever --steps is.
+REFERENCE_SECONDS = 10.0
+
+
 def run_reference(args, rank: int, world: int) -> dict | None:
     if rank != 0:
         return None
@@ -281,14 +285,21 @@ def run_reference(args, rank: int, world: int) -> dict | None:
     threads = _host_threads()
     calls = WORKLOADS[config]["calls"]
     cases = [_case(config, seed=layer, dcp_rank=0) for layer in range(calls)]
-    for _ in range(args.warmup):
+    for _ in range(max(1, args.warmup)):
         _oracle_step(cases, threads)
+    # A step is `reps` full workload steps, sized so that the K timed steps
+    # take about REFERENCE_SECONDS in all: a window of a few milliseconds
+    # (20 single calls) measured host noise, not the port.
+    t0 = time.perf_counter()
+    _oracle_step(cases, threads)
+    one = time.perf_counter() - t0
+    reps = max(1, math.ceil(REFERENCE_SECONDS / (args.steps * max(one, 1e-6))))
     start = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(args.steps * reps):
         _oracle_step(cases, threads)
     elapsed = time.perf_counter() - start
     per_step = elapsed / args.steps
-    indices = calls * cases[0].batch * cases[0].width
+    indices = reps * calls * cases[0].batch * cases[0].width
     value = indices / per_step / 1e9
     return {
         "impl": "reference",
@@ -299,7 +310,7 @@ def run_reference(args, rank: int, world: int) -> dict | None:
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": per_step * 1e3,
-        "us_per_call": per_step * 1e6 / calls,
+        "us_per_call": per_step * 1e6 / (reps * calls),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -311,8 +322,9 @@ def run_reference(args, rank: int, world: int) -> dict | None:
             "unit": UNIT,
             "cores": threads,
             "kind": "port",
-            "sample": f"{args.steps} full steps, {threads} threads (C restatement of "
-                      "silkern/contract.py:67-158 in oracle/localize_oracle.c)",
+            "sample": f"{args.steps} steps of {reps} full workload steps ({reps * calls} call(s) of "
+                      f"{cases[0].batch}x{cases[0].width}) in {elapsed:.2f} s, {threads} threads (C "
+                      "restatement of silkern/contract.py:67-158 in oracle/localize_oracle.c)",
         },
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
