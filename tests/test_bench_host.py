@@ -102,6 +102,23 @@ def test_reference_arm_line_on_cpu() -> None:
     assert line["e2e"]["h2d_bytes_per_step"] == 0
 
 
+def test_reference_arm_steps_are_calibrated_samples(monkeypatch) -> None:
+    """A reference step is R whole calls, R sized so the K steps take about
+    REFERENCE_SECONDS; the line's rate, per-step and per-call times agree."""
+    import argparse
+    import re
+
+    monkeypatch.setattr(bench, "REFERENCE_SECONDS", 0.5)
+    args = argparse.Namespace(config=3, steps=4, warmup=1)
+    line = bench.run_reference(args, 0, 1)
+    reps = int(re.search(r"of (\d+) full workload steps", line["cpu_baseline"]["sample"]).group(1))
+    assert reps >= 1 and line["steps"] == 4
+    indices = 256 * 2048
+    assert line["value"] == pytest.approx(reps * indices / (line["ms_per_step"] * 1e-3) / 1e9, rel=1e-9)
+    assert line["us_per_call"] == pytest.approx(line["ms_per_step"] * 1e3 / reps, rel=1e-9)
+    assert line["e2e"]["value"] == line["value"] == line["cpu_baseline"]["value"]
+
+
 def test_reference_arm_other_ranks_print_nothing() -> None:
     env = dict(os.environ, RANK="1", WORLD_SIZE="2")
     proc = subprocess.run(
